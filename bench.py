@@ -1,0 +1,392 @@
+#!/usr/bin/env python3
+"""Benchmark of the FlashVSR B200 operator pack (one JSON line on rank 0).
+
+Metric: DiT tokens/s @1408x768 on B200.  A step is one steady-
+state FlashVSR streaming chunk through the 30-block FlashVSR-Tiny-shaped DiT
+(dim 1536, 12 heads x 128, FFN 8960; f=2 latent frames x 48 x 88 = 8448 tokens
+= 8 output frames; KV cache of 3 time rows, so attention sees 264 key windows;
+keep rule: own time row + top 25% of past windows by mean-pooled q.k), every op
+on this pack's sm_100a kernels, the step replayed as one CUDA graph.  Random-init
+weights (N(0, 0.02)), synthetic N(0,1) inputs.
+
+  python bench.py [--gpus N --steps K --warmup W]          # this pack
+  python bench.py --impl reference [...]                    # the reference path on CPU
+
+With N > 1 (torchrun) every rank renders its own tile stream of the same shape
+(tiles are independent; "scaling": "weak") and value = all tokens / max-over-
+ranks time.  The reference arm times the reference's torch-eager formulas (the
+CPU oracle restated from the reference, since the reference's own kernels are
+Triton and need a GPU) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+H_PX, W_PX = 768, 1408
+BLOCKS = 30
+D, HEADS, FFN = 1536, 12, 8960
+CTX = 512
+KV_LEN = 3
+RATIO = 0.25
+METRIC = "DiT tokens/s @1408x768 (30-block FlashVSR-Tiny DiT, streaming f=2 step)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--blocks", type=int, default=BLOCKS)
+    p.add_argument("--no-graph", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def config(args, world):
+    lat_h, lat_w = H_PX // 16, W_PX // 16
+    return {
+        "workload": "dit30_1408x768_stream_f2",
+        "tokens_per_step": 2 * lat_h * lat_w,
+        "frames_per_step": 8,
+        "blocks": args.blocks,
+        "dim": D, "heads": HEADS, "ffn": FFN, "context_tokens": CTX,
+        "kv_cache_rows": KV_LEN, "query_windows": lat_h // 8 * (lat_w // 8),
+        "key_windows": (KV_LEN + 1) * (lat_h // 8) * (lat_w // 8),
+        "keep_rule": f"own time row + top {int(RATIO * 100)}% past windows (mean-pooled q.k)",
+        "fp8_scales": "per-token activations x per-channel weights",
+        "parallelism": f"tile-replica x{world}",
+        "global_batch": world,
+        "seq_len": 2 * lat_h * lat_w,
+        "l2_policy": "inputs larger than L2: 1.39 GB of FP8 weights stream through each step",
+        "cuda_graph": not args.no_graph,
+    }
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            return None
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        loaded = [s for s in sm if smax and s > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_block_sample(steps=1, warm=True):
+    """Reference formulas on the host: one DiT block at the step's exact shape.
+
+    Returns (seconds per block, threads)."""
+    from oracle import ops as O
+    from oracle import wan
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    lat_h, lat_w = H_PX // 16, W_PX // 16
+    P = wan.init_block_params(g, D, FFN)
+    Q = wan.quantize_block(P, "token")
+    L = 2 * lat_h * lat_w
+    x = torch.randn(1, L, D, generator=g).to(torch.bfloat16)
+    t_mod = torch.randn(1, 6, D, generator=g).to(torch.bfloat16)
+    ctx = torch.randn(1, CTX, D, generator=g).to(torch.bfloat16)
+    kv = wan.cross_kv(Q, ctx)
+    per_row = (lat_h // 8) * (lat_w // 8)
+    cache = (torch.randn(KV_LEN * per_row, 128, D, generator=g).to(torch.bfloat16),
+             torch.randn(KV_LEN * per_row, 128, D, generator=g).to(torch.bfloat16))
+    cos, sin = O.freqs_cos_sin(wan.grid_freqs(2, lat_h, lat_w, f0=6))
+    mask_fn = wan.causal_mask_fn(HEADS, per_row, RATIO)
+    run = lambda: wan.block_forward(Q, x, t_mod, cos, sin, (2, lat_h, lat_w), kv, mask_fn,  # noqa: E731
+                                    HEADS, cache, KV_LEN)
+    if warm:
+        run()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run()
+    return (time.perf_counter() - t0) / steps, torch.get_num_threads()
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    cfg = config(args, world)
+    tokens = cfg["tokens_per_step"]
+    for _ in range(max(args.warmup, 0) and 1):
+        cpu_block_sample(steps=1, warm=False)
+    times = []
+    budget = 240.0
+    t_start = time.perf_counter()
+    for i in range(args.steps):
+        t, threads = cpu_block_sample(steps=1, warm=False)
+        times.append(t)
+        if time.perf_counter() - t_start > budget:
+            break
+    per_block = statistics.mean(times)
+    step_s = per_block * args.blocks
+    value = tokens / step_s
+    sample = (f"{len(times)} timed DiT block forwards of the step shape ({tokens} tokens, 264 key "
+              f"windows), x{args.blocks} blocks per step; torch-eager reference formulas on "
+              f"{cpu_model()}")
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": len(times), "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 (fp8 fake-quant linears)", "data": "synthetic", "config": cfg,
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- B200 arm
+def attention_roofline(runner, iters, stream):
+    """Time the dominant kernel (block-sparse attention at the step's shape) with CUDA events."""
+    from flashvsr_sm89_ops_b200 import lcsa
+    dev = runner.device
+    g = torch.Generator(device=dev).manual_seed(11)
+    per_row = runner.h // 8 * (runner.w // 8)
+    nq, nk = per_row, (KV_LEN + 1) * per_row
+    q = torch.randn(nq * 128, D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(nk * 128, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(nk * 128, D, generator=g, device=dev).to(torch.bfloat16)
+    keep = lcsa.causal_topk_mask(q, k, HEADS, per_row, RATIO)
+    sel, cnt, _ = lcsa.build_csr(keep)
+    pairs = int(keep.sum().item())
+    out = torch.empty_like(q)
+    for _ in range(3):
+        lcsa.attention_csr(q, k, v, sel, cnt, HEADS, out=out)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        lcsa.attention_csr(q, k, v, sel, cnt, HEADS, out=out)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / iters
+    flops = pairs * 4 * 128 * 128 * 128
+    return ms, flops, pairs
+
+
+def traffic_from_profiles(kernel):
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            d = json.load(f)
+        return d.get(kernel, {}).get("bytes_per_launch")
+    except Exception:
+        return None
+
+
+def run_b200(args, world, rank, local_rank):
+    import torch.distributed as dist
+    from flashvsr_sm89_ops_b200 import _lib
+    from flashvsr_sm89_ops_b200.runner import StreamingDiT
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    runner = StreamingDiT(num_layers=args.blocks, dim=D, heads=HEADS, ffn=FFN, height=H_PX,
+                          width=W_PX, ctx_len=CTX, kv_len=KV_LEN, mask_rule="causal",
+                          seed=rank, device=dev)
+    runner.prime()
+    tokens = runner.tokens(2)
+    x_static = runner.make_input(2)
+    stream = torch.cuda.current_stream(dev)
+
+    # launches of this pack's kernels per step (counted on one eager step)
+    _lib.start_launch_count()
+    runner.step(x_static)
+    launches = _lib.stop_launch_count()
+    torch.cuda.synchronize(dev)
+
+    if args.no_graph:
+        step = lambda: runner.step(x_static)  # noqa: E731
+        y = runner.step(x_static)
+    else:
+        graph, y = runner.capture(x_static)
+        step = graph.replay
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * tokens * args.steps / (ms_max / 1e3)
+
+    # end to end through the public API: pinned host input -> step -> host output
+    x_host = torch.empty(x_static.shape, dtype=x_static.dtype, pin_memory=True)
+    x_host.copy_(x_static.cpu())
+    y_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+    for _ in range(2):
+        x_static.copy_(x_host, non_blocking=True)
+        step()
+        y_host.copy_(y, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(args.steps):
+        x_static.copy_(x_host, non_blocking=True)
+        step()
+        y_host.copy_(y, non_blocking=True)
+    e3.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t2 = torch.tensor([e2.elapsed_time(e3)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e = world * tokens * args.steps / (float(t2.item()) / 1e3)
+
+    # roofline of the dominant kernel, timed live with CUDA events on the launching stream
+    att_ms, att_flops, pairs = attention_roofline(runner, max(args.steps, 10), stream)
+    peaks, peak_kind = load_peaks()
+    achieved = att_flops / (att_ms / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    devs = _lib.device_error()
+    if devs:
+        raise RuntimeError(f"device error word set: {devs:#x}")
+
+    if rank != 0:
+        return
+    cfg = config(args, world)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8_e4m3 GEMMs + bf16 attention/norms", "data": "synthetic (random-init weights, N(0,1) inputs)",
+        "config": cfg,
+        "fps": world * 8 * args.steps / (ms_max / 1e3),
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": x_static.numel() * 2,
+                "d2h_bytes_per_step": y.numel() * 2},
+        "gpu_launches": launches * args.steps,
+        "roofline": {"kernel": "bsa_fwd_kernel (block-sparse attention, 91,080 kept window pairs)",
+                     "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_kind": f"{peak_kind} bf16 dense (burst)",
+                     "traffic": traffic_from_profiles("bsa_fwd_kernel"),
+                     "launch_ms": att_ms, "flops_per_launch": att_flops},
+        "clocks": clocks,
+    }
+    if world == 1 and os.environ.get("FVB_SKIP_CPU_BASELINE") != "1":
+        t_block, threads = cpu_block_sample(steps=1, warm=False)
+        cpu_value = tokens / (t_block * args.blocks)
+        line["cpu_baseline"] = {
+            "value": cpu_value, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"1 DiT block forward of the step shape on the host ({cpu_model()}), "
+                      f"scaled to {args.blocks} blocks"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, world, rank)  # rank 0 only; other ranks exit without work
+        return
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_b200(args, world, rank, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

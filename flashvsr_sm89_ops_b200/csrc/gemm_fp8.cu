@@ -1,0 +1,355 @@
+// FP8 E4M3 GEMM on the 5th-generation tensor cores (a3), with the scale /
+// bias epilogue of FP8Linear._mm (fp8_linear.py:28-30) and an optional fused
+// GELU(tanh) + row-amax epilogue for the FFN up-projection (fp8_ffn.py:24-40).
+//
+//   out[m, n] = bf16(acc[m, n] * sa[m|0] * sw[n|0] + bias[n]),  acc = sum_k A[m,k] W[n,k]
+//
+// Design (one persistent CTA per SM, 192 threads, warp-specialised):
+//   warp 0      TMA producer: 128x128-byte A tiles and BNx128-byte W tiles
+//               (128-byte swizzle) into a 4-stage shared-memory ring
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma kind::f8f6f4
+//               (M=128, N=BN, K=32 per instruction) into a TMEM accumulator;
+//               tcgen05.commit releases ring stages and publishes finished tiles.
+//               Also allocates / frees the 2*BN TMEM columns.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (each thread owns one
+//               output row), apply scales + bias (+ GELU / amax), store bf16.
+// The accumulator is double-buffered in TMEM so the epilogue of tile t overlaps
+// the main loop of tile t+1.  Both operands are K-major ("TN"), exactly the
+// nn.Linear weight layout, so no transpose is ever materialised.
+#include "common.cuh"
+
+namespace fvb {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 128;  // bytes == fp8 elements per K block
+constexpr int STAGES = 4;
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
+
+struct Args {
+  int M, N, K;
+  const float* sa;
+  const float* sw;
+  int a_row, w_row;
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  float* amax_out;
+};
+
+template <int BN>
+constexpr size_t smem_bytes() {
+  return (size_t)STAGES * (BM + BN) * BK + 1024 /*align slack*/ + 256 /*barriers*/;
+}
+
+__device__ __forceinline__ float gelu_tanh_bf16_epi(float x) {
+  const float kBeta = 0.7978845608028654f;
+  const float kKappa = 0.044715f;
+  float x3 = x * x * x;
+  float inner = kBeta * __fmaf_rn(kKappa, x3, x);
+  return bf16r(0.5f * x * (1.0f + tanhf(inner)));
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  uint8_t* sA = base;
+  uint8_t* sB = sA + STAGES * BM * BK;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * BN * BK);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = warp_id_uniform();
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (args.M + BM - 1) / BM;
+  const int n_tiles = (args.N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kblocks = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], EPI_WARPS);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * BM;
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, 0x101u)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], (uint32_t)((BM + BN) * BK));
+          tma_load_2d(sA + stage * BM * BK, &tmA, &full[stage], kb * BK, m0);
+          tma_load_2d(sB + stage * BN * BK, &tmB, &full[stage], kb * BK, n0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(0 /*E4M3*/, 0 /*E4M3*/, 0, 0, BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
+        const int buf = t & 1;
+        const uint32_t tph = (uint32_t)(t >> 1) & 1u;
+        if (!mbar_wait(&tempty[buf], tph ^ 1u, 0x102u)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, 0x103u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * BM * BK);
+          const uint32_t b0 = smem_u32(sB + stage * BN * BK);
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            const uint64_t da = smem_desc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t db = smem_desc_sw128(b0 + k * 32, 16, 1024);
+            mma_f8f6f4(d_tmem, da, db, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) tc_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int t = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+      const int buf = t & 1;
+      const uint32_t tph = (uint32_t)(t >> 1) & 1u;
+      const int m0 = (tile / n_tiles) * BM;
+      const int n0 = (tile % n_tiles) * BN;
+      if (!mbar_wait(&tfull[buf], tph, 0x104u)) break;
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < args.M;
+      const float sa = args.a_row ? (row_ok ? __ldg(args.sa + row) : 0.f) : __ldg(args.sa);
+      const float sw0 = args.w_row ? 0.f : __ldg(args.sw);
+      float tmax = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 32), r);
+        tmem_ld_wait();
+        const int col0 = n0 + c * 32;
+        if (row_ok) {
+          __nv_bfloat16* orow = args.out + (int64_t)row * args.ldo;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int cg = col0 + g * 8;
+            if (cg < args.N) {
+              float v[8];
+              float swv[8], bv[8];
+              if (args.w_row) {
+                const float4 s0 = __ldg(reinterpret_cast<const float4*>(args.sw + cg));
+                const float4 s1 = __ldg(reinterpret_cast<const float4*>(args.sw + cg + 4));
+                swv[0] = s0.x; swv[1] = s0.y; swv[2] = s0.z; swv[3] = s0.w;
+                swv[4] = s1.x; swv[5] = s1.y; swv[6] = s1.z; swv[7] = s1.w;
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) swv[i] = sw0;
+              }
+              if (args.bias) {
+                bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(args.bias + cg)), bv);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) bv[i] = 0.f;
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                float o = __fmaf_rn(__uint_as_float(r[g * 8 + i]), sa * swv[i], bv[i]);
+                if (EPI == FVB_EPI_GELU_AMAX) {
+                  o = gelu_tanh_bf16_epi(bf16r(o));
+                  tmax = fmaxf(tmax, fabsf(o));
+                }
+                v[i] = o;
+              }
+              *reinterpret_cast<uint4*>(orow + cg) = f32_to_bf16x8(v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      if (EPI == FVB_EPI_GELU_AMAX) {
+        if (args.a_row) {
+          if (row_ok) atomic_max_nonneg(args.amax_out + row, tmax);
+        } else {
+          tmax = warp_max(tmax);
+          if (lane == 0) atomic_max_nonneg(args.amax_out, tmax);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
+template <int BN, int EPI>
+static int launch(const Args& a, const void* A, const void* W, cudaStream_t st) {
+  CUtensorMap tmA, tmB;
+  int rc = make_tmap_2d(&tmA, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.M,
+                        (uint64_t)a.K, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.N,
+                    (uint64_t)a.K, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  auto kern = fp8_gemm_kernel<BN, EPI>;
+  constexpr size_t smem = smem_bytes<BN>();
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    FVB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "fp8 gemm smem attribute");
+    configured[dev] = true;
+  }
+  const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+  int grid = sm_count();
+  if (tiles < grid) grid = tiles;
+  kern<<<grid, THREADS, smem, st>>>(tmA, tmB, a);
+  return check_launch("fvb_fp8_gemm");
+}
+
+// choose the N tile: fewer partial waves wins, 256 on ties
+static int pick_bn(int M, int N) {
+  const int sms = sm_count();
+  auto eff = [&](int bn) {
+    long tiles = (long)((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+    long waves = (tiles + sms - 1) / sms;
+    // useful columns / computed columns, times wave occupancy
+    double col_eff = (double)N / (double)(((N + bn - 1) / bn) * bn);
+    return col_eff * (double)tiles / (double)(waves * sms);
+  };
+  return eff(128) > eff(256) * 1.02 ? 128 : 256;
+}
+
+}  // namespace gemm
+}  // namespace fvb
+
+extern "C" {
+
+int fvb_fp8_gemm(const void* A, const float* sa, int a_mode, const void* W, const float* sw,
+                 int w_mode, const void* bias, int64_t M, int64_t N, int64_t K, void* out,
+                 int epilogue, float* amax_out, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(M >= 0 && N >= 0 && K >= 0, "fvb_fp8_gemm: negative size");
+  FVB_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "fvb_fp8_gemm: size");
+  FVB_REQUIRE(a_mode == FVB_SCALE_TENSOR || a_mode == FVB_SCALE_ROW, "fvb_fp8_gemm: a_mode");
+  FVB_REQUIRE(w_mode == FVB_SCALE_TENSOR || w_mode == FVB_SCALE_ROW, "fvb_fp8_gemm: w_mode");
+  FVB_REQUIRE(epilogue == FVB_EPI_NONE || epilogue == FVB_EPI_GELU_AMAX, "fvb_fp8_gemm: epilogue");
+  if (M == 0 || N == 0) return FVB_OK;
+  FVB_REQUIRE(K > 0 && K % 16 == 0, "fvb_fp8_gemm: K=%lld must be a positive multiple of 16",
+              (long long)K);
+  FVB_REQUIRE(N % 8 == 0, "fvb_fp8_gemm: N=%lld must be a multiple of 8", (long long)N);
+  FVB_REQUIRE(A && W && sa && sw && out, "fvb_fp8_gemm: NULL pointer");
+  FVB_REQUIRE(aligned16(A) && aligned16(W) && aligned16(out) && (!bias || aligned16(bias)),
+              "fvb_fp8_gemm: A, W, out and bias must be 16-byte aligned");
+  FVB_REQUIRE(w_mode != FVB_SCALE_ROW || aligned16(sw), "fvb_fp8_gemm: sw alignment");
+  FVB_REQUIRE(epilogue == FVB_EPI_NONE || amax_out != nullptr, "fvb_fp8_gemm: amax_out is NULL");
+  gemm::Args a;
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.sa = sa;
+  a.sw = sw;
+  a.a_row = a_mode == FVB_SCALE_ROW;
+  a.w_row = w_mode == FVB_SCALE_ROW;
+  a.bias = (const __nv_bfloat16*)bias;
+  a.out = (__nv_bfloat16*)out;
+  a.ldo = N;
+  a.amax_out = amax_out;
+  const int bn = gemm::pick_bn(a.M, a.N);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (epilogue == FVB_EPI_NONE)
+    return bn == 128 ? gemm::launch<128, FVB_EPI_NONE>(a, A, W, st)
+                     : gemm::launch<256, FVB_EPI_NONE>(a, A, W, st);
+  return bn == 128 ? gemm::launch<128, FVB_EPI_GELU_AMAX>(a, A, W, st)
+                   : gemm::launch<256, FVB_EPI_GELU_AMAX>(a, A, W, st);
+}
+
+size_t fvb_fp8_ffn_workspace_bytes(int64_t M, int64_t F) {
+  // h (bf16 [M,F]) + h8 (fp8 [M,F]) + amax [M] + h scale [M], each 256-aligned
+  auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+  return up((size_t)M * F * 2) + up((size_t)M * F) + up((size_t)(M > 0 ? M : 1) * 4) * 2;
+}
+
+int fvb_fp8_ffn(const void* x8, const float* sx, int mode, const void* W0, const float* sw0,
+                const void* b0, const void* W2, const float* sw2, const void* b2, int w_mode,
+                int64_t M, int64_t D, int64_t F, void* out, void* workspace,
+                fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(M >= 0 && D > 0 && F > 0, "fvb_fp8_ffn: shape");
+  if (M == 0) return FVB_OK;
+  FVB_REQUIRE(workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+              "fvb_fp8_ffn: workspace must be 256-byte aligned");
+  auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* h = ws;
+  void* h8 = ws + up((size_t)M * F * 2);
+  float* amax = reinterpret_cast<float*>(ws + up((size_t)M * F * 2) + up((size_t)M * F));
+  float* hs = amax + up((size_t)M * 4) / 4;
+  const size_t namax = (mode == FVB_SCALE_ROW) ? (size_t)M : 1;
+  cudaStream_t st = (cudaStream_t)stream;
+  FVB_CUDA_TRY(cudaMemsetAsync(amax, 0, namax * sizeof(float), st), "fvb_fp8_ffn amax clear");
+  int rc = fvb_fp8_gemm(x8, sx, mode, W0, sw0, w_mode, b0, M, F, D, h, FVB_EPI_GELU_AMAX, amax,
+                        stream);
+  if (rc) return rc;
+  rc = fvb_quant_fp8_with_amax(h, M, F, amax, mode, h8, hs, stream);
+  if (rc) return rc;
+  return fvb_fp8_gemm(h8, hs, mode, W2, sw2, w_mode, b2, M, D, F, out, FVB_EPI_NONE, nullptr,
+                      stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,388 @@
+// Layout and block-mask kernels around the block-sparse attention:
+//   a14  window partition / reverse (raster <-> (2,8,8)-window order)
+//   a11  keep mask -> CSR, on the device and without the reference's host sync
+//   a13  draft_block_mask (reference selection semantics), and the causal top-k
+//        rule of the benchmark configuration
+#include "common.cuh"
+
+namespace fvb {
+
+// ---------------------------------------------------------------------------
+// a14: window partition.  Token rows of C bf16 are permuted, one warp per row.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) window_kernel(const uint4* __restrict__ x, int64_t xvec_ld,
+                                                      int64_t rows,
+                                                      int64_t F, int64_t Hh, int64_t Ww,
+                                                      int64_t cvec, int wf, int wh, int ww,
+                                                      int reverse, uint4* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t o = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (o >= rows) return;
+  // decompose the window-order index o
+  const int64_t wsize = (int64_t)wf * wh * ww;
+  const int64_t nF = F / wf, nH = Hh / wh, nW = Ww / ww;
+  int64_t t = o;
+  const int64_t inwin = t % wsize;
+  t /= wsize;
+  const int64_t wi = t % nW;
+  t /= nW;
+  const int64_t hi = t % nH;
+  t /= nH;
+  const int64_t fi = t % nF;
+  const int64_t b = t / nF;
+  const int64_t a = inwin / ((int64_t)wh * ww);
+  const int64_t c = (inwin / ww) % wh;
+  const int64_t d = inwin % ww;
+  const int64_t r = ((b * F + fi * wf + a) * Hh + hi * wh + c) * Ww + wi * ww + d;  // raster row
+  const int64_t src = reverse ? o : r;
+  const int64_t dst = reverse ? r : o;
+  const uint4* s = x + src * xvec_ld;
+  uint4* dd = out + dst * cvec;
+  for (int64_t v = lane; v < cvec; v += 32) dd[v] = __ldg(s + v);
+}
+
+// ---------------------------------------------------------------------------
+// a11: keep [H*NQ, NK] -> sel (kept ascending, then unkept ascending), cnt
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) mask_to_csr_kernel(const uint8_t* __restrict__ keep,
+                                                           int64_t nrows, int64_t NK,
+                                                           int32_t* __restrict__ sel,
+                                                           int32_t* __restrict__ cnt) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= nrows) return;
+  const uint8_t* kr = keep + row * NK;
+  int32_t* sr = sel + row * NK;
+  const unsigned lt = (1u << lane) - 1u;
+  int base = 0;
+  for (int64_t k0 = 0; k0 < NK; k0 += 32) {
+    const int64_t k = k0 + lane;
+    const bool on = (k < NK) && kr[k] != 0;
+    const unsigned bal = __ballot_sync(0xffffffffu, on);
+    if (on) sr[base + __popc(bal & lt)] = (int32_t)k;
+    base += __popc(bal);
+  }
+  if (lane == 0) cnt[row] = base;
+  for (int64_t k0 = 0; k0 < NK; k0 += 32) {
+    const int64_t k = k0 + lane;
+    const bool off = (k < NK) && kr[k] == 0;
+    const unsigned bal = __ballot_sync(0xffffffffu, off);
+    if (off) sr[base + __popc(bal & lt)] = (int32_t)k;
+    base += __popc(bal);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// block pooling: mean over the 128 tokens of each window, per channel.
+// round_bf16 mirrors torch.mean on a bf16 tensor (fp32 accumulate, bf16 result).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) pool_kernel(const __nv_bfloat16* __restrict__ x,
+                                                    int64_t nblk, int64_t C, int round_bf16,
+                                                    float* __restrict__ avg) {
+  const int64_t blk = blockIdx.x;
+  if (blk >= nblk) return;
+  const __nv_bfloat16* xb = x + blk * 128 * C;
+  for (int64_t c8 = threadIdx.x; c8 * 8 < C; c8 += blockDim.x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int t = 0; t < 128; ++t) {
+      float f[8];
+      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(xb + t * C) + c8), f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += f[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float m = __fdiv_rn(acc[i], 128.0f);
+      avg[blk * C + c8 * 8 + i] = round_bf16 ? bf16r(m) : m;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// a13 step 2: per (head, query block) scores over all key blocks, local mask,
+// softmax -> probabilities (bf16-rounded like the bf16 reference tensors).
+// grid (NQ, H), block 256; dynamic smem NK floats.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) draft_scores_kernel(
+    const float* __restrict__ aq, const float* __restrict__ ak, int64_t NQ, int64_t NK, int H,
+    int d, const uint8_t* __restrict__ local, int64_t sq, int64_t sk, float* __restrict__ prob) {
+  extern __shared__ float sc[];
+  __shared__ float red[32];
+  const int64_t qi = blockIdx.x;
+  const int h = blockIdx.y;
+  const int64_t C = (int64_t)H * d;
+  const float* qv = aq + qi * C + (int64_t)h * d;
+  const float inv_sqrt_d = 1.0f / sqrtf((float)d);  // python float 1/sqrt(D) in the reference
+  const float sqrt_d = sqrtf((float)d);
+  (void)inv_sqrt_d;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  // one warp per key block: dot product over d
+  for (int64_t kj = wid; kj < NK; kj += nw) {
+    const float* kv = ak + kj * C + (int64_t)h * d;
+    float acc = 0.f;
+    for (int e = lane; e < d; e += 32) acc = __fmaf_rn(qv[e], kv[e], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      // einsum output is bf16, then "/ math.sqrt(D)" -> bf16
+      float s = bf16r(__fdiv_rn(bf16r(acc), sqrt_d));
+      const bool on = local[(qi % sq) * sk + (kj % sk)] != 0;
+      sc[kj] = on ? s : -INFINITY;
+    }
+  }
+  __syncthreads();
+  float m = -INFINITY;
+  for (int64_t kj = threadIdx.x; kj < NK; kj += blockDim.x) m = fmaxf(m, sc[kj]);
+  m = warp_max(m);
+  if (lane == 0) red[wid] = m;
+  __syncthreads();
+  if (wid == 0) {
+    float t = lane < nw ? red[lane] : -INFINITY;
+    t = warp_max(t);
+    if (lane == 0) red[0] = t;
+  }
+  __syncthreads();
+  m = red[0];
+  __syncthreads();
+  float s = 0.f;
+  for (int64_t kj = threadIdx.x; kj < NK; kj += blockDim.x) {
+    float e = (sc[kj] == -INFINITY) ? 0.f : expf(sc[kj] - m);
+    sc[kj] = e;
+    s += e;
+  }
+  s = warp_sum(s);
+  if (lane == 0) red[wid] = s;
+  __syncthreads();
+  if (wid == 0) {
+    float t = lane < nw ? red[lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float tot = red[0];
+  float* pr = prob + ((int64_t)h * NQ + qi) * NK;
+  for (int64_t kj = threadIdx.x; kj < NK; kj += blockDim.x) pr[kj] = bf16r(__fdiv_rn(sc[kj], tot));
+}
+
+// ---------------------------------------------------------------------------
+// a13 step 3: joint top-k per (head, query time row): threshold = the (k+1)-th
+// largest probability of the flattened [per_row, NK] slab, keep = prob > thr.
+// Probabilities are non-negative bf16 values, so their 16-bit patterns order
+// like unsigned integers: a two-pass (high byte, low byte) radix select finds
+// the exact threshold.  grid (q_temporal, H), block 1024.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) draft_topk_kernel(const float* __restrict__ prob,
+                                                           int64_t NQ, int64_t NK,
+                                                           int64_t per_row, int64_t topk,
+                                                           uint8_t* __restrict__ keep) {
+  __shared__ unsigned hist[256];
+  __shared__ unsigned sel_hi, sel_lo, rank_left;
+  const int64_t t = blockIdx.x;
+  const int h = blockIdx.y;
+  const int64_t n = per_row * NK;
+  const float* p = prob + ((int64_t)h * NQ + t * per_row) * NK;
+  uint8_t* kp = keep + ((int64_t)h * NQ + t * per_row) * NK;
+  int64_t apply = topk < n - 1 ? topk : n - 1;
+  if (apply < 0) apply = 0;
+  const unsigned k = (unsigned)(apply + 1);  // 1-indexed rank from the top
+  // pass 1: high byte
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    unsigned b = __float_as_uint(p[i]) >> 16;  // bf16 bit pattern
+    atomicAdd(&hist[(b >> 8) & 0xFF], 1u);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned acc = 0, bin = 0;
+    for (int b = 255; b >= 0; --b) {
+      if (acc + hist[b] >= k) {
+        bin = (unsigned)b;
+        break;
+      }
+      acc += hist[b];
+    }
+    sel_hi = bin;
+    rank_left = k - acc;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    unsigned b = __float_as_uint(p[i]) >> 16;
+    if (((b >> 8) & 0xFF) == sel_hi) atomicAdd(&hist[b & 0xFF], 1u);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned acc = 0, bin = 0;
+    for (int b = 255; b >= 0; --b) {
+      if (acc + hist[b] >= rank_left) {
+        bin = (unsigned)b;
+        break;
+      }
+      acc += hist[b];
+    }
+    sel_lo = bin;
+  }
+  __syncthreads();
+  const unsigned thr_bits = (sel_hi << 8) | sel_lo;
+  const float thr = __uint_as_float(thr_bits << 16);
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) kp[i] = p[i] > thr ? 1 : 0;
+}
+
+// ---------------------------------------------------------------------------
+// causal top-k rule (benchmark measurement input).  grid (NQ, H), block 256,
+// dynamic smem 2*NK floats.  Scores use fp32 pooled means.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) causal_topk_kernel(const float* __restrict__ aq,
+                                                           const float* __restrict__ ak,
+                                                           int64_t NQ, int64_t NK, int H, int d,
+                                                           int64_t per_row, float ratio,
+                                                           uint8_t* __restrict__ keep) {
+  extern __shared__ float sc[];
+  const int64_t qi = blockIdx.x;
+  const int h = blockIdx.y;
+  const int64_t C = (int64_t)H * d;
+  const int64_t cache_rows = (NK - NQ) / per_row;
+  const int64_t qrow = cache_rows + qi / per_row;  // global time row of the query block
+  const int64_t npast = qrow * per_row;            // key blocks in earlier rows
+  const int64_t nsel = (int64_t)floorf(ratio * (float)npast);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const float* qv = aq + qi * C + (int64_t)h * d;
+  for (int64_t kj = wid; kj < npast; kj += nw) {
+    const float* kv = ak + kj * C + (int64_t)h * d;
+    float acc = 0.f;
+    for (int e = lane; e < d; e += 32) acc = __fmaf_rn(qv[e], kv[e], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) sc[kj] = acc;
+  }
+  __syncthreads();
+  uint8_t* kp = keep + ((int64_t)h * NQ + qi) * NK;
+  for (int64_t kj = threadIdx.x; kj < NK; kj += blockDim.x) {
+    const int64_t krow = kj / per_row;
+    uint8_t on = 0;
+    if (krow == qrow) {
+      on = 1;
+    } else if (krow < qrow) {
+      // rank among past blocks: larger score first, ties by lower index
+      const float s = sc[kj];
+      int64_t rank = 0;
+      for (int64_t o = 0; o < npast; ++o) {
+        const float so = sc[o];
+        rank += (so > s) || (so == s && o < kj);
+      }
+      on = rank < nsel;
+    }
+    kp[kj] = on;
+  }
+}
+
+static inline unsigned warp_rows_grid(int64_t rows) { return (unsigned)((rows + 7) / 8); }
+
+}  // namespace fvb
+
+extern "C" {
+
+int fvb_window_partition(const void* x, int64_t x_ld, int64_t B, int64_t F, int64_t Hh,
+                         int64_t Ww, int64_t C, int wf, int wh, int ww, int reverse, void* out,
+                         fvb_stream_t stream) {
+  using namespace fvb;
+  if (x_ld == 0) x_ld = C;
+  FVB_REQUIRE(B >= 0 && F >= 0 && Hh >= 0 && Ww >= 0 && C > 0, "fvb_window_partition: shape");
+  FVB_REQUIRE(wf > 0 && wh > 0 && ww > 0 && F % wf == 0 && Hh % wh == 0 && Ww % ww == 0,
+              "fvb_window_partition: (F,H,W)=(%lld,%lld,%lld) not divisible by window (%d,%d,%d)",
+              (long long)F, (long long)Hh, (long long)Ww, wf, wh, ww);
+  FVB_REQUIRE(C % 8 == 0 && x_ld >= C && x_ld % 8 == 0,
+              "fvb_window_partition: C and x_ld must be multiples of 8, x_ld >= C");
+  const int64_t rows = B * F * Hh * Ww;
+  if (rows == 0) return FVB_OK;
+  FVB_REQUIRE(x && out && aligned16(x) && aligned16(out), "fvb_window_partition: pointers");
+  FVB_REQUIRE(x != out, "fvb_window_partition: in-place not supported");
+  window_kernel<<<warp_rows_grid(rows), 256, 0, (cudaStream_t)stream>>>(
+      (const uint4*)x, x_ld / 8, rows, F, Hh, Ww, C / 8, wf, wh, ww, reverse, (uint4*)out);
+  return check_launch("fvb_window_partition");
+}
+
+int fvb_mask_to_csr(const uint8_t* keep, int64_t H, int64_t NQ, int64_t NK, int32_t* sel,
+                    int32_t* cnt, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(H >= 0 && NQ >= 0 && NK >= 0, "fvb_mask_to_csr: shape");
+  const int64_t rows = H * NQ;
+  if (rows == 0) return FVB_OK;
+  FVB_REQUIRE(keep && sel && cnt, "fvb_mask_to_csr: NULL pointer");
+  mask_to_csr_kernel<<<warp_rows_grid(rows), 256, 0, (cudaStream_t)stream>>>(keep, rows, NK, sel,
+                                                                             cnt);
+  return check_launch("fvb_mask_to_csr");
+}
+
+size_t fvb_draft_mask_workspace_bytes(int64_t H, int64_t NQ, int64_t NK, int64_t d) {
+  // pooled q [NQ, H*d] + pooled k [NK, H*d] + probabilities [H, NQ, NK], fp32
+  size_t b = (size_t)(NQ + NK) * H * d * 4 + (size_t)H * NQ * NK * 4;
+  return (b + 255) & ~(size_t)255;
+}
+
+int fvb_draft_block_mask(const void* q_w, const void* k_w, int64_t H, int64_t NQ, int64_t NK,
+                         int64_t d, const uint8_t* local, int64_t sq, int64_t sk,
+                         int64_t q_temporal, int64_t topk, uint8_t* keep, void* workspace,
+                         fvb_stream_t stream) {
+  using namespace fvb;
+  cudaStream_t st = (cudaStream_t)stream;
+  FVB_REQUIRE(H > 0 && NQ > 0 && NK > 0 && d > 0 && (H * d) % 8 == 0, "fvb_draft_block_mask: shape");
+  FVB_REQUIRE(sq > 0 && sk > 0 && NQ % sq == 0 && NK % sk == 0,
+              "fvb_draft_block_mask: local mask [%lld,%lld] must tile [%lld,%lld]", (long long)sq,
+              (long long)sk, (long long)NQ, (long long)NK);
+  FVB_REQUIRE(q_temporal > 0 && NQ % q_temporal == 0, "fvb_draft_block_mask: q_temporal");
+  FVB_REQUIRE(q_w && k_w && local && keep && workspace, "fvb_draft_block_mask: NULL pointer");
+  FVB_REQUIRE(aligned16(q_w) && aligned16(k_w), "fvb_draft_block_mask: alignment");
+  FVB_REQUIRE(NK * 4 <= 200 * 1024, "fvb_draft_block_mask: NK too large");
+  const int64_t C = H * d;
+  float* aq = static_cast<float*>(workspace);
+  float* ak = aq + NQ * C;
+  float* prob = ak + NK * C;
+  pool_kernel<<<(unsigned)NQ, 192, 0, st>>>((const __nv_bfloat16*)q_w, NQ, C, 1, aq);
+  pool_kernel<<<(unsigned)NK, 192, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 1, ak);
+  int rc = check_launch("fvb_draft_block_mask pool");
+  if (rc) return rc;
+  const size_t smem = (size_t)NK * 4;
+  if (smem > 48 * 1024)
+    FVB_CUDA_TRY(cudaFuncSetAttribute(draft_scores_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "draft_scores smem");
+  draft_scores_kernel<<<dim3((unsigned)NQ, (unsigned)H), 256, smem, st>>>(
+      aq, ak, NQ, NK, (int)H, (int)d, local, sq, sk, prob);
+  rc = check_launch("fvb_draft_block_mask scores");
+  if (rc) return rc;
+  draft_topk_kernel<<<dim3((unsigned)q_temporal, (unsigned)H), 1024, 0, st>>>(
+      prob, NQ, NK, NQ / q_temporal, topk, keep);
+  return check_launch("fvb_draft_block_mask topk");
+}
+
+int fvb_causal_topk_mask(const void* q_w, const void* k_w, int64_t H, int64_t NQ, int64_t NK,
+                         int64_t d, int64_t per_row, float ratio, uint8_t* keep, void* workspace,
+                         fvb_stream_t stream) {
+  using namespace fvb;
+  cudaStream_t st = (cudaStream_t)stream;
+  FVB_REQUIRE(H > 0 && NQ > 0 && NK >= NQ && d > 0 && (H * d) % 8 == 0,
+              "fvb_causal_topk_mask: shape");
+  FVB_REQUIRE(per_row > 0 && NQ % per_row == 0 && NK % per_row == 0,
+              "fvb_causal_topk_mask: blocks per time row must divide NQ and NK");
+  FVB_REQUIRE(q_w && k_w && keep && workspace, "fvb_causal_topk_mask: NULL pointer");
+  FVB_REQUIRE(aligned16(q_w) && aligned16(k_w), "fvb_causal_topk_mask: alignment");
+  FVB_REQUIRE(NK * 4 <= 200 * 1024, "fvb_causal_topk_mask: NK too large");
+  const int64_t C = H * d;
+  float* aq = static_cast<float*>(workspace);
+  float* ak = aq + NQ * C;
+  pool_kernel<<<(unsigned)NQ, 192, 0, st>>>((const __nv_bfloat16*)q_w, NQ, C, 0, aq);
+  pool_kernel<<<(unsigned)NK, 192, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 0, ak);
+  int rc = check_launch("fvb_causal_topk_mask pool");
+  if (rc) return rc;
+  const size_t smem = (size_t)NK * 4;
+  if (smem > 48 * 1024)
+    FVB_CUDA_TRY(cudaFuncSetAttribute(causal_topk_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "causal_topk smem");
+  causal_topk_kernel<<<dim3((unsigned)NQ, (unsigned)H), 256, smem, st>>>(
+      aq, ak, NQ, NK, (int)H, (int)d, per_row, ratio, keep);
+  return check_launch("fvb_causal_topk_mask");
+}
+
+}  // extern "C"

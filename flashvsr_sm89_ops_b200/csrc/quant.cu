@@ -1,0 +1,277 @@
+// FP8 E4M3 activation quantisation (a1), GELU(tanh)->FP8 (a5) and the
+// quantise-with-known-amax pass of the FFN mid-section.
+//
+// Numerics follow flashvsr_sm89_ops/fp8_quant.py:25-35 and fp8_ffn.py:24-54:
+//   s = max(amax, 1e-12) / 448   (fp32, IEEE divide)
+//   q = e4m3_rn_satfinite(clamp(x / s, -448, 448))   (IEEE divide, never x * (1/s))
+//   returned scale = amax / 448
+// amax is order-independent, so codes and scales are bit-exact against any
+// correct implementation of the same formula.
+//
+// Layout: x [M, K] bf16 row-major.  Per-token mode gives each row its own
+// scale; rows are handled one warp each with 16-byte vector loads, the row
+// held in registers when K <= 2048 and re-read from L1/L2 otherwise.
+#include "common.cuh"
+
+namespace fvb {
+
+constexpr float kFp8Max = 448.0f;
+
+// GELU with the tanh approximation, evaluated like PyTorch's CUDA kernel for
+// F.gelu(approximate="tanh") on a bf16 tensor: fp32 math, result rounded to
+// bf16 (fp8_ffn.py:24-30 mirrors the same bf16 output rounding).
+__device__ __forceinline__ float gelu_tanh_bf16(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
+  const float kKappa = 0.044715f;
+  float x3 = x * x * x;
+  float inner = kBeta * __fmaf_rn(kKappa, x3, x);
+  float y = 0.5f * x * (1.0f + tanhf(inner));
+  return bf16r(y);
+}
+
+__device__ __forceinline__ float quant_scale_from_amax(float amax) {
+  return __fdiv_rn(fmaxf(amax, 1e-12f), kFp8Max);
+}
+
+__device__ __forceinline__ float clamp448(float v) { return fminf(fmaxf(v, -kFp8Max), kFp8Max); }
+
+// 8 values -> 8 e4m3 codes packed in a uint2
+__device__ __forceinline__ uint2 quant8(const float* f, float s) {
+  uint32_t w[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint16_t lo = f32x2_to_e4m3x2(clamp448(__fdiv_rn(f[4 * h + 0], s)),
+                                  clamp448(__fdiv_rn(f[4 * h + 1], s)));
+    uint16_t hi = f32x2_to_e4m3x2(clamp448(__fdiv_rn(f[4 * h + 2], s)),
+                                  clamp448(__fdiv_rn(f[4 * h + 3], s)));
+    w[h] = (uint32_t)lo | ((uint32_t)hi << 16);
+  }
+  return make_uint2(w[0], w[1]);
+}
+
+template <bool GELU>
+__device__ __forceinline__ void load8(const uint4* src, int64_t v, float* f) {
+  uint4 u = __ldg(src + v);
+  bf16x8_to_f32(u, f);
+  if (GELU) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = gelu_tanh_bf16(f[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// per-tensor: pass 1 = global amax (atomic max on the bit pattern), pass 2 = quantise
+// ---------------------------------------------------------------------------
+template <bool GELU>
+__global__ void __launch_bounds__(256) absmax_kernel(const uint4* __restrict__ x, int64_t nvec,
+                                                      const __nv_bfloat16* __restrict__ xs,
+                                                      int64_t n, float* __restrict__ amax) {
+  float m = 0.f;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    float f[8];
+    load8<GELU>(x, v, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+  }
+  // scalar tail (n % 8)
+  if (blockIdx.x == 0) {
+    for (int64_t i = nvec * 8 + threadIdx.x; i < n; i += blockDim.x) {
+      float f = __bfloat162float(xs[i]);
+      if (GELU) f = gelu_tanh_bf16(f);
+      m = fmaxf(m, fabsf(f));
+    }
+  }
+  m = warp_max(m);
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_max(t);
+    if (threadIdx.x == 0) atomic_max_nonneg(amax, t);
+  }
+}
+
+template <bool GELU>
+__global__ void __launch_bounds__(256) quant_tensor_kernel(
+    const uint4* __restrict__ x, int64_t nvec, const __nv_bfloat16* __restrict__ xs, int64_t n,
+    const float* __restrict__ amax_p, uint2* __restrict__ q, uint8_t* __restrict__ qs,
+    float* __restrict__ scale_out) {
+  const float amax = *amax_p;
+  const float s = quant_scale_from_amax(amax);
+  if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = __fdiv_rn(amax, kFp8Max);
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    float f[8];
+    load8<GELU>(x, v, f);
+    q[v] = quant8(f, s);
+  }
+  if (blockIdx.x == 0) {
+    for (int64_t i = nvec * 8 + threadIdx.x; i < n; i += blockDim.x) {
+      float f = __bfloat162float(xs[i]);
+      if (GELU) f = gelu_tanh_bf16(f);
+      qs[i] = f32_to_e4m3(clamp448(__fdiv_rn(f, s)));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// per-token: one warp per row
+// ---------------------------------------------------------------------------
+template <bool GELU, int NV>
+__global__ void __launch_bounds__(256) quant_row_kernel(const __nv_bfloat16* __restrict__ x,
+                                                         int64_t M, int64_t K,
+                                                         uint8_t* __restrict__ q,
+                                                         float* __restrict__ scale_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const __nv_bfloat16* xr = x + row * K;
+  uint8_t* qr = q + row * K;
+  const int64_t nvec = K >> 3;  // K % 8 == 0 enforced by the host
+  const uint4* xv = reinterpret_cast<const uint4*>(xr);
+  uint2* qv = reinterpret_cast<uint2*>(qr);
+  float m = 0.f;
+  if constexpr (NV > 0) {
+    float f[NV][8];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      int64_t v = (int64_t)j * 32 + lane;
+      if (v < nvec) {
+        load8<GELU>(xv, v, f[j]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[j][i]));
+      }
+    }
+    m = warp_max(m);
+    const float s = quant_scale_from_amax(m);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      int64_t v = (int64_t)j * 32 + lane;
+      if (v < nvec) qv[v] = quant8(f[j], s);
+    }
+  } else {
+    for (int64_t v = lane; v < nvec; v += 32) {
+      float f[8];
+      load8<GELU>(xv, v, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+    }
+    m = warp_max(m);
+    const float s = quant_scale_from_amax(m);
+    for (int64_t v = lane; v < nvec; v += 32) {
+      float f[8];
+      load8<GELU>(xv, v, f);
+      qv[v] = quant8(f, s);
+    }
+  }
+  if (lane == 0) scale_out[row] = __fdiv_rn(m, kFp8Max);
+}
+
+// quantise with a known amax ([1] per-tensor or [M] per-row); flat, vectorised
+__global__ void __launch_bounds__(256) quant_with_amax_kernel(
+    const uint4* __restrict__ g, int64_t M, int64_t K, const float* __restrict__ amax, int per_row,
+    uint2* __restrict__ q, float* __restrict__ scale_out) {
+  const int64_t kv = K >> 3;
+  const int64_t nvec = M * kv;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    int64_t row = per_row ? v / kv : 0;
+    float a = __ldg(amax + row);
+    float f[8];
+    bf16x8_to_f32(__ldg(g + v), f);
+    q[v] = quant8(f, quant_scale_from_amax(a));
+    if (per_row ? (v % kv == 0) : (v == 0)) scale_out[row] = __fdiv_rn(a, kFp8Max);
+  }
+}
+
+static int grid_for(int64_t nvec, int threads) {
+  int64_t blocks = (nvec + threads - 1) / threads;
+  int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+template <bool GELU>
+static int quant_impl(const void* x, int64_t M, int64_t K, void* q, float* scale_out, int mode,
+                      void* workspace, cudaStream_t st, const char* name) {
+  FVB_REQUIRE(M >= 0 && K >= 0, "%s: negative size", name);
+  FVB_REQUIRE(mode == FVB_SCALE_TENSOR || mode == FVB_SCALE_ROW, "%s: bad mode %d", name, mode);
+  FVB_REQUIRE(scale_out != nullptr, "%s: scale_out is NULL", name);
+  const int64_t n = M * K;
+  if (n == 0) {
+    // reference: empty input -> empty codes and a zero scale (fp8_quant.py:45-47)
+    int64_t ns = (mode == FVB_SCALE_ROW) ? M : 1;
+    if (ns > 0) FVB_CUDA_TRY(cudaMemsetAsync(scale_out, 0, ns * sizeof(float), st), name);
+    return FVB_OK;
+  }
+  FVB_REQUIRE(x && q, "%s: NULL pointer", name);
+  FVB_REQUIRE(aligned16(x), "%s: x not 16-byte aligned", name);
+  if (mode == FVB_SCALE_ROW) {
+    FVB_REQUIRE(K % 8 == 0, "%s: per-token mode needs K %% 8 == 0 (K=%lld)", name, (long long)K);
+    FVB_REQUIRE((reinterpret_cast<uintptr_t>(q) & 7u) == 0, "%s: q not 8-byte aligned", name);
+    const int rows_per_block = 8;
+    dim3 grid((unsigned)((M + rows_per_block - 1) / rows_per_block));
+    if (K <= 2048)
+      quant_row_kernel<GELU, 8><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, M, K,
+                                                       (uint8_t*)q, scale_out);
+    else
+      quant_row_kernel<GELU, 0><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, M, K,
+                                                       (uint8_t*)q, scale_out);
+    return check_launch(name);
+  }
+  FVB_REQUIRE(workspace != nullptr, "%s: per-tensor mode needs a workspace", name);
+  FVB_REQUIRE((reinterpret_cast<uintptr_t>(q) & 7u) == 0, "%s: q not 8-byte aligned", name);
+  float* amax = static_cast<float*>(workspace);
+  FVB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(float), st), name);
+  const int64_t nvec = n >> 3;
+  const int g = grid_for(nvec > 0 ? nvec : 1, 256);
+  absmax_kernel<GELU><<<g, 256, 0, st>>>((const uint4*)x, nvec, (const __nv_bfloat16*)x, n, amax);
+  int rc = check_launch(name);
+  if (rc) return rc;
+  quant_tensor_kernel<GELU><<<g, 256, 0, st>>>((const uint4*)x, nvec, (const __nv_bfloat16*)x, n,
+                                               amax, (uint2*)q, (uint8_t*)q, scale_out);
+  return check_launch(name);
+}
+
+}  // namespace fvb
+
+extern "C" {
+
+size_t fvb_quant_fp8_workspace_bytes(int64_t M, int64_t K, int mode) {
+  (void)M;
+  (void)K;
+  return mode == FVB_SCALE_TENSOR ? 256 : 0;
+}
+
+int fvb_quant_fp8(const void* x, int64_t M, int64_t K, void* q, float* scale_out, int mode,
+                  void* workspace, fvb_stream_t stream) {
+  return fvb::quant_impl<false>(x, M, K, q, scale_out, mode, workspace, (cudaStream_t)stream,
+                                "fvb_quant_fp8");
+}
+
+int fvb_gelu_quant_fp8(const void* h, int64_t M, int64_t K, void* q, float* scale_out, int mode,
+                       void* workspace, fvb_stream_t stream) {
+  return fvb::quant_impl<true>(h, M, K, q, scale_out, mode, workspace, (cudaStream_t)stream,
+                               "fvb_gelu_quant_fp8");
+}
+
+int fvb_quant_fp8_with_amax(const void* g, int64_t M, int64_t K, const float* amax, int mode,
+                            void* q, float* scale_out, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(M >= 0 && K >= 0, "fvb_quant_fp8_with_amax: negative size");
+  FVB_REQUIRE(mode == FVB_SCALE_TENSOR || mode == FVB_SCALE_ROW, "fvb_quant_fp8_with_amax: mode");
+  if (M * K == 0) return FVB_OK;
+  FVB_REQUIRE(g && amax && q && scale_out, "fvb_quant_fp8_with_amax: NULL pointer");
+  FVB_REQUIRE(K % 8 == 0, "fvb_quant_fp8_with_amax: K %% 8 != 0");
+  FVB_REQUIRE(aligned16(g) && (reinterpret_cast<uintptr_t>(q) & 7u) == 0,
+              "fvb_quant_fp8_with_amax: misaligned pointer");
+  const int64_t nvec = M * K / 8;
+  quant_with_amax_kernel<<<grid_for(nvec, 256), 256, 0, (cudaStream_t)stream>>>(
+      (const uint4*)g, M, K, amax, mode == FVB_SCALE_ROW, (uint2*)q, scale_out);
+  return check_launch("fvb_quant_fp8_with_amax");
+}
+
+}  // extern "C"

@@ -1,0 +1,74 @@
+"""Fused AdaLN elementwise chains on the sm_100a library.
+
+Drop-in for ``flashvsr_sm89_ops.fused_adaln`` (fused_adaln.py:60-85):
+``fused_ln_modulate(x, scale, shift, eps)`` (note: scale BEFORE shift) and
+``fused_gate_add(x, gate, residual)``, with the reference's per-op bf16 rounding
+chain (gate-add is bitwise equal to eager).  ``fused_ln_modulate(...,
+emit_fp8=True)`` also returns the per-token E4M3 codes and scales of its
+output, so the following FP8 linear skips its own quantisation pass.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _check(x, name):
+    _lib.require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"{name}: expected bf16, got {x.dtype}")
+
+
+def fused_ln_modulate(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
+                      eps: float = 1e-6, emit_fp8: bool = False, out: torch.Tensor | None = None):
+    """LayerNorm(affine=False) + modulate. x [B, L, D] contiguous bf16; scale/shift [B, 1, D]."""
+    _check(x, "fused_ln_modulate")
+    B, L, D = x.shape
+    assert x.is_contiguous() and scale.is_contiguous() and shift.is_contiguous()
+    if scale.dtype != torch.bfloat16 or shift.dtype != torch.bfloat16:
+        raise ValueError("fused_ln_modulate: scale/shift must be bf16")
+    if scale.numel() != B * D or shift.numel() != B * D:
+        raise ValueError("fused_ln_modulate: scale/shift must be [B, 1, D]")
+    if out is None:
+        out = torch.empty_like(x)
+    q8 = qs = None
+    if emit_fp8:
+        q8 = torch.empty((B * L, D), dtype=torch.float8_e4m3fn, device=x.device)
+        qs = torch.empty((B * L,), dtype=torch.float32, device=x.device)
+    _lib.call("fvb_ln_modulate", _lib.ptr(x), _lib.ptr(scale), _lib.ptr(shift), B, L, D,
+              float(eps), _lib.ptr(out), _lib.ptr(q8), _lib.ptr(qs), _lib.stream_of(x))
+    if emit_fp8:
+        return out, q8, qs
+    return out
+
+
+def fused_gate_add(x: torch.Tensor, gate: torch.Tensor | None, residual: torch.Tensor,
+                   out: torch.Tensor | None = None):
+    """x + gate * residual. x/residual [B, L, D] contiguous bf16; gate [B, 1, D] (None: x + r)."""
+    _check(x, "fused_gate_add")
+    B, L, D = x.shape
+    assert x.is_contiguous() and residual.is_contiguous() and (gate is None or gate.is_contiguous())
+    if residual.dtype != torch.bfloat16 or (gate is not None and gate.dtype != torch.bfloat16):
+        raise ValueError("fused_gate_add: gate/residual must be bf16")
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.call("fvb_gate_add", _lib.ptr(x), _lib.ptr(gate), _lib.ptr(residual), B, L, D,
+              _lib.ptr(out), _lib.stream_of(x))
+    return out
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None,
+               eps: float = 1e-6, out: torch.Tensor | None = None):
+    """torch.nn.LayerNorm semantics (fp32 math, one bf16 rounding) over the last dim."""
+    _check(x, "layer_norm")
+    D = x.shape[-1]
+    x = x.contiguous()
+    rows = x.numel() // D
+    w = weight.to(torch.bfloat16).contiguous() if weight is not None else None
+    b = bias.to(torch.bfloat16).contiguous() if bias is not None else None
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.call("fvb_layer_norm", _lib.ptr(x), _lib.ptr(w), _lib.ptr(b), rows, D, float(eps),
+              _lib.ptr(out), _lib.stream_of(x))
+    return out

@@ -1,0 +1,202 @@
+"""Spatially tiled rendering, sharded over the GPUs of one box.
+
+Drop-in for ``flashvsr_sm89_ops.tiling`` (tiling.py:19-205): the same module
+constants, ``plan_tiles`` / ``tile_weight`` / ``auto_tile_limits`` /
+``render_tiled`` with identical plans and weights (the planner is a pure
+function of the canvas, so it must agree exactly).  The B200 changes are in
+``render_tiled``:
+  * blending happens on the GPU in fp32 (the reference blends on the host,
+    tiling.py:203), so a tile's frames never leave HBM until the end;
+  * under ``torch.distributed`` with world size N > 1, tile i is rendered by rank
+    i % N, each rank accumulates its weighted tiles into its own partial canvas,
+    and one ``dist.reduce`` (NCCL over NVLink on GPUs, gloo on CPU) sums the
+    partial canvases into rank 0.  The weights form a partition of unity, so the
+    sum is the blended canvas.  Rank 0 returns it; the other ranks return None.
+"""
+from __future__ import annotations
+
+import torch
+
+MULT = 128                # pipeline output grid (px)
+OVERLAP = 256             # shared pixels between neighbouring tiles
+TILE_THRESHOLD = 2_200_000
+TILE_TARGET = 2_100_000
+_GIB_PER_MP = 8.6
+_REFERENCE_FRAMES = 85
+_SAFETY_GIB = 1.25
+_TILE_FLOOR = 640_000
+
+
+def _round_up(v: int, mult: int = MULT) -> int:
+    return ((v + mult - 1) // mult) * mult
+
+
+def _limits_for_free_bytes(free_bytes, num_frames=_REFERENCE_FRAMES, safety_gib=_SAFETY_GIB):
+    """(threshold, target) for `free_bytes` of device memory, or None if nothing is left.
+
+    Same VRAM model as tiling.py:45-61: activation GiB per output megapixel scales
+    linearly with the frame count; target is clamped to [floor, TILE_TARGET] and
+    the threshold follows it down.
+    """
+    usable = free_bytes - int(safety_gib * (1 << 30))
+    if usable <= 0:
+        return None
+    per_mp = _GIB_PER_MP * max(num_frames, 1) / _REFERENCE_FRAMES
+    tgt = int(usable / (per_mp * (1 << 30)) * 1e6)
+    tgt = max(min(TILE_TARGET, tgt), _TILE_FLOOR)
+    return min(TILE_THRESHOLD, tgt), tgt
+
+
+def auto_tile_limits(num_frames=_REFERENCE_FRAMES, device="cuda", safety_gib=_SAFETY_GIB):
+    """(threshold, target) sized to the memory actually free now (tiling.py:64-82)."""
+    if device != "cuda" or not torch.cuda.is_available():
+        return TILE_THRESHOLD, TILE_TARGET
+    try:
+        torch.cuda.empty_cache()
+        free, _ = torch.cuda.mem_get_info()
+    except Exception:
+        return TILE_THRESHOLD, TILE_TARGET
+    lim = _limits_for_free_bytes(free, num_frames, safety_gib)
+    return lim if lim is not None else (TILE_THRESHOLD, TILE_TARGET)
+
+
+def _strip_starts(canvas, piece, n):
+    """Offsets of n pieces covering [0, canvas): evenly strided, last one flush right."""
+    step = (canvas - piece) // (n - 1)
+    out = [k * step for k in range(n - 1)]
+    out.append(canvas - piece)
+    return out
+
+
+def _piece(canvas, n, overlap):
+    return _round_up((canvas + (n - 1) * overlap + n - 1) // n)
+
+
+def plan_tiles(W, H, target=TILE_TARGET, threshold=TILE_THRESHOLD, overlap=OVERLAP, mult=MULT):
+    """Cover W x H with overlapping tiles on the mult grid -> [(x, y, w, h), ...].
+
+    Order of preference (tiling.py:96-137): the full frame when W*H <= threshold;
+    2..8 full-height vertical strips; 2..8 full-width horizontal strips; otherwise
+    a cols x rows grid (2..6 each) with the fewest seams, then the fewest pieces.
+    """
+    if W * H <= threshold:
+        return [(0, 0, W, H)]
+    smallest = overlap + mult
+
+    def usable(p, canvas, cross):
+        return smallest <= p <= canvas and p * cross <= target
+
+    for n in range(2, 9):
+        p = _piece(W, n, overlap)
+        if usable(p, W, H):
+            return [(x, 0, p, H) for x in _strip_starts(W, p, n)]
+    for n in range(2, 9):
+        p = _piece(H, n, overlap)
+        if usable(p, H, W):
+            return [(0, y, W, p) for y in _strip_starts(H, p, n)]
+    choice = None
+    for cols in range(2, 7):
+        for rows in range(2, 7):
+            pw, ph = _piece(W, cols, overlap), _piece(H, rows, overlap)
+            if pw * ph > target or pw < smallest or ph < smallest:
+                continue
+            rank = (cols + rows - 2, cols * rows)
+            if choice is None or rank < choice[0]:
+                choice = (rank, pw, ph, cols, rows)
+    if choice is None:
+        raise ValueError(f"cannot tile {W}x{H} into ~{target} px pieces")
+    _, pw, ph, cols, rows = choice
+    return [(x, y, pw, ph) for y in _strip_starts(H, ph, rows) for x in _strip_starts(W, pw, cols)]
+
+
+def _axis_weights(starts, piece):
+    """Per-piece 1-D weights: linear ramps across each shared span, summing to 1."""
+    ws = []
+    last = len(starts) - 1
+    for i, s in enumerate(starts):
+        w = torch.ones(piece, dtype=torch.float32)
+        if i > 0:
+            span = starts[i - 1] + piece - s
+            w[:span] = torch.linspace(0.0, 1.0, span + 2)[1:-1]
+        if i < last:
+            span = s + piece - starts[i + 1]
+            w[piece - span:] = torch.linspace(1.0, 0.0, span + 2)[1:-1]
+        ws.append(w)
+    return ws
+
+
+def tile_weight(x, y, tiles):
+    """Blending weight of the tile at (x, y) as an [h, w] map; all tiles sum to 1."""
+    xs = sorted({t[0] for t in tiles})
+    ys = sorted({t[1] for t in tiles})
+    wx = _axis_weights(xs, tiles[0][2])[xs.index(x)]
+    wy = _axis_weights(ys, tiles[0][3])[ys.index(y)]
+    return wy[:, None] * wx[None, :]
+
+
+def assign_tiles(n_tiles: int, world: int, rank: int):
+    """Tile indices rendered by `rank` (round-robin; every tile exactly once)."""
+    return list(range(rank, n_tiles, world))
+
+
+def _dist_info(group):
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_world_size(group), dist.get_rank(group)
+    return 1, 0
+
+
+def render_tiled(pipe, lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
+                 tile_threshold=TILE_THRESHOLD, device=None, group=None, **pipe_kwargs):
+    """Render lq_video [C,F,H,W] (or [1,C,F,H,W], in [-1, 1]) through `pipe` one tile at a time.
+
+    Same contract as tiling.py:164-205: per-tile LQ crop, height/width and an
+    area-scaled topk_ratio; returns [C, F', H, W] in lq_video's dtype.  Blending
+    runs on `device` (default: this rank's CUDA device, else CPU).  With a
+    process group of N ranks each rank renders tiles i % N == rank and rank 0
+    returns the reduced canvas (other ranks return None).
+    """
+    import torch.distributed as dist
+
+    batched = lq_video.dim() == 5
+    lq = lq_video[0] if batched else lq_video
+    C, F, H, W = lq.shape
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    pipe_kwargs.setdefault("num_frames", F)
+    tiles = plan_tiles(W, H, target=tile_target, threshold=tile_threshold, overlap=overlap)
+    world, rank = _dist_info(group)
+    if len(tiles) == 1 and world == 1:
+        return pipe(LQ_video=lq_video.to(device), height=H, width=W, **pipe_kwargs)
+
+    num_frames = pipe_kwargs.pop("num_frames")
+    base_topk = pipe_kwargs.pop("topk_ratio", None)
+    mine = assign_tiles(len(tiles), world, rank)
+    canvas = None
+    n_out = torch.zeros(1, dtype=torch.int64, device=device)
+    for i in mine:
+        x, y, w, h = tiles[i]
+        crop = lq[:, :, y:y + h, x:x + w].to(device, non_blocking=True)
+        extra = {"topk_ratio": base_topk * (W * H) / (w * h)} if base_topk is not None else {}
+        frames = pipe(LQ_video=crop.unsqueeze(0) if batched else crop, num_frames=num_frames,
+                      height=h, width=w, **extra, **pipe_kwargs)
+        if canvas is None:
+            canvas = torch.zeros((C, frames.shape[-3], H, W), dtype=torch.float32, device=device)
+            n_out.fill_(frames.shape[-3])
+        elif canvas.shape[1] != frames.shape[-3]:
+            raise RuntimeError(f"tile frame counts diverge: {canvas.shape[1]} vs {frames.shape[-3]}")
+        wgt = tile_weight(x, y, tiles).to(device)
+        canvas[:, :, y:y + h, x:x + w] += frames.to(device=device, dtype=torch.float32) * wgt
+        del frames
+    if world == 1:
+        return canvas.to(dtype=lq_video.dtype)
+    # every rank needs the output frame count to size its (possibly empty) canvas
+    dist.all_reduce(n_out, op=dist.ReduceOp.MAX, group=group)
+    if canvas is None:
+        canvas = torch.zeros((C, int(n_out.item()), H, W), dtype=torch.float32, device=device)
+    elif canvas.shape[1] != int(n_out.item()):
+        raise RuntimeError(f"rank {rank}: tile frame count {canvas.shape[1]} != {int(n_out.item())}")
+    dist.reduce(canvas, dst=0, op=dist.ReduceOp.SUM, group=group)
+    if rank == 0:
+        return canvas.to(dtype=lq_video.dtype)
+    return None

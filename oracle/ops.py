@@ -1,0 +1,296 @@
+"""CPU restatement of the reference operator formulas (test infrastructure only).
+
+All functions take and return CPU tensors.  bf16 rounding points are placed
+exactly where the reference kernels place them.  Citations are paths inside
+aireet/flashvsr-sm89-ops.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+FP8_MAX = 448.0  # flashvsr_sm89_ops/fp8_quant.py:13
+E4M3 = torch.float8_e4m3fn
+
+
+# ----------------------------------------------------------------------------- FP8
+def quantize_fp8(x2: torch.Tensor, mode: str = "tensor"):
+    """Activation quantisation of flashvsr_sm89_ops/fp8_quant.py:42-55 (kernels :16-35).
+
+    amax = max|x| (fp32); s = max(amax, 1e-12)/448; q = e4m3(clamp(x/s, +-448)) with an
+    fp32 IEEE divide and round-to-nearest-even; the returned scale is amax/448.
+    mode "token" applies the same formula to each row (the per-token granularity the
+    B200 pack adds; no reference counterpart beyond the formula).
+    """
+    xf = x2.float()
+    if mode == "tensor":
+        if xf.numel() == 0:
+            return x2.to(E4M3), torch.zeros(1)
+        amax = xf.abs().amax().reshape(1)
+    else:
+        if xf.numel() == 0:
+            return x2.to(E4M3), torch.zeros(xf.shape[0])
+        amax = xf.abs().amax(dim=-1)
+    s = torch.clamp(amax, min=1e-12) / FP8_MAX
+    sb = s if mode == "tensor" else s[:, None]
+    q = torch.clamp(xf / sb, -FP8_MAX, FP8_MAX).to(E4M3)
+    return q, amax / FP8_MAX
+
+
+def gelu_tanh(h: torch.Tensor) -> torch.Tensor:
+    """GELU(tanh) with a bf16 result, the oracle fp8_ffn.py:7-10,24-30 targets."""
+    return F.gelu(h, approximate="tanh")
+
+
+def gelu_quant_fp8(h: torch.Tensor, mode: str = "tensor"):
+    """fused_gelu_quant_fp8 (fp8_ffn.py:57-72) == quantize_fp8(gelu(h)) (its docstring :58-60)."""
+    return quantize_fp8(gelu_tanh(h), mode)
+
+
+def fp8_weight(w: torch.Tensor, mode: str = "tensor"):
+    """One-time weight quantisation of FP8Linear.__init__ (fp8_linear.py:17-22).
+
+    w_scale = (|w|.amax()/448).clamp(min=1e-12) (fp32); codes = (w / w_scale).to(e4m3),
+    evaluated in the weight's own dtype exactly like the eager expression (a bf16 weight
+    divides to bf16 before the e4m3 cast).  mode "channel": one scale per output row.
+    """
+    if mode == "tensor":
+        s = (w.abs().amax() / FP8_MAX).clamp(min=1e-12).float()
+        q = (w / s).to(E4M3)
+        return q, s.reshape(1)
+    s = (w.abs().amax(dim=1) / FP8_MAX).clamp(min=1e-12).float()
+    q = (w / s[:, None]).to(E4M3)
+    return q, s
+
+
+def fp8_mm(qa, sa, qw, sw, bias=None):
+    """FP8Linear._mm = torch._scaled_mm(x8, W.t(), scale_a, scale_b, bias, bf16) (fp8_linear.py:28-30).
+
+    Restated as an fp32 product of the decoded codes, scaled per row of A and per row of
+    W, plus bias, rounded once to bf16.
+    """
+    acc = qa.float() @ qw.float().t()
+    sa_ = sa.reshape(-1, 1) if sa.numel() > 1 else sa.reshape(1, 1)
+    sw_ = sw.reshape(1, -1) if sw.numel() > 1 else sw.reshape(1, 1)
+    y = acc * (sa_ * sw_)
+    if bias is not None:
+        y = y + bias.float()
+    return y.to(torch.bfloat16)
+
+
+def fp8_linear(x, qw, sw, bias=None, act_mode="tensor"):
+    """FP8Linear.forward (fp8_linear.py:32-42): quantise the activation, then _mm."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    qa, sa = quantize_fp8(x2, act_mode)
+    y = fp8_mm(qa, sa, qw, sw, bias)
+    return y.reshape(*shape[:-1], y.shape[-1])
+
+
+def fp8_ffn(x, qw0, sw0, b0, qw2, sw2, b2, act_mode="tensor"):
+    """FP8FFN.forward (fp8_ffn.py:84-96): quant -> mm0 -> GELU + quant -> mm2."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    qa, sa = quantize_fp8(x2, act_mode)
+    h = fp8_mm(qa, sa, qw0, sw0, b0)
+    qh, sh = gelu_quant_fp8(h, act_mode)
+    out = fp8_mm(qh, sh, qw2, sw2, b2)
+    return out.reshape(*shape[:-1], out.shape[-1])
+
+
+# ----------------------------------------------------------------------------- norms
+def freqs_cos_sin(freqs: torch.Tensor):
+    """_freqs_cos_sin (fused_rms_rope.py:58-63): complex [..., S, half] -> fp32 cos, sin [S, half]."""
+    fr = torch.view_as_real(freqs.reshape(-1, freqs.shape[-1]))
+    return fr[..., 0].float().contiguous(), fr[..., 1].float().contiguous()
+
+
+def rms_rope(x, weight, cos=None, sin=None, eps=1e-6, rope=True, head_dim=128):
+    """_rms_rope_kernel (fused_rms_rope.py:21-55) for x [B, L, D] bf16.
+
+    rrms = 1/sqrt(mean(x^2) + eps) (fp32); y = bf16(x * rrms) * w (fp32);
+    pairs (2i, 2i+1) of each head: even -> y_e c - y_o s, odd -> y_o c + y_e s with
+    (c, s) = cos/sin[l, i]; one bf16 rounding at the end.
+    """
+    B, L, D = x.shape
+    xf = x.float()
+    ms = (xf * xf).sum(-1, keepdim=True) / D
+    rrms = 1.0 / torch.sqrt(ms + eps)
+    y = (xf * rrms).to(torch.bfloat16).float() * weight.float()
+    if not rope:
+        return y.to(torch.bfloat16)
+    half = head_dim // 2
+    yp = y.view(B, L, D // head_dim, half, 2)
+    c = cos.view(1, L, 1, half)
+    s = sin.view(1, L, 1, half)
+    ye, yo = yp[..., 0], yp[..., 1]
+    oe = ye * c + yo * (-s)
+    oo = yo * c + ye * s
+    return torch.stack([oe, oo], dim=-1).view(B, L, D).to(torch.bfloat16)
+
+
+def ln_modulate(x, scale, shift, eps=1e-6):
+    """_ln_modulate_kernel (fused_adaln.py:22-42): LN without affine then modulate.
+
+    xn = bf16((x - mean)/sqrt(var + eps)); y = bf16(bf16(xn * bf16(1 + scale)) + shift).
+    x [B, L, D]; scale, shift [B, 1, D].  Note the argument order (scale before shift).
+    """
+    xf = x.float()
+    D = x.shape[-1]
+    mean = xf.sum(-1, keepdim=True) / D
+    var = ((xf - mean) ** 2).sum(-1, keepdim=True) / D
+    xn = ((xf - mean) / torch.sqrt(var + eps)).to(torch.bfloat16).float()
+    one_plus = (1.0 + scale.float()).to(torch.bfloat16).float()
+    y = (xn * one_plus).to(torch.bfloat16).float()
+    return (y + shift.float()).to(torch.bfloat16)
+
+
+def gate_add(x, gate, residual):
+    """_gate_add_kernel (fused_adaln.py:45-57): bf16(x + bf16(g * r)), bitwise = eager x + g*r."""
+    y = (gate.float() * residual.float()).to(torch.bfloat16).float()
+    return (x.float() + y).to(torch.bfloat16)
+
+
+def layer_norm(x, weight, bias, eps=1e-6):
+    """torch.nn.LayerNorm on bf16 (the DiT block's norm3; eager in the reference)."""
+    return F.layer_norm(x.float(), (x.shape[-1],), weight.float() if weight is not None else None,
+                        bias.float() if bias is not None else None, eps).to(torch.bfloat16)
+
+
+# ----------------------------------------------------------------------------- LCSA
+def window_partition(x, win=(2, 8, 8)):
+    """WindowPartition3D.partition (lcsa/reference.py:15-21): [B,F,H,W,C] -> [Nwin, wf*wh*ww, C]."""
+    B, Fr, H, W, C = x.shape
+    wf, wh, ww = win
+    t = x.reshape(B, Fr // wf, wf, H // wh, wh, W // ww, ww, C)
+    t = t.permute(0, 1, 3, 5, 2, 4, 6, 7)
+    return t.reshape(-1, wf * wh * ww, C)
+
+
+def window_reverse(xw, win, fhw, B=1):
+    """Inverse of window_partition (upstream WindowPartition3D.reverse, integrate.py:117-120)."""
+    Fr, H, W = fhw
+    wf, wh, ww = win
+    C = xw.shape[-1]
+    t = xw.reshape(B, Fr // wf, H // wh, W // ww, wf, wh, ww, C)
+    t = t.permute(0, 1, 4, 2, 5, 3, 6, 7)
+    return t.reshape(B, Fr, H, W, C)
+
+
+def local_block_mask(bh, bw, rng):
+    """build_local_block_mask (lcsa/reference.py:24-34): window of side rng centred at each block."""
+    idx = torch.arange(bh * bw)
+    r, c = idx // bw, idx % bw
+    r0 = r - rng // 2
+    c0 = c - rng // 2
+    in_r = (r[None, :] >= r0[:, None]) & (r[None, :] <= r0[:, None] + rng - 1)
+    in_c = (c[None, :] >= c0[:, None]) & (c[None, :] <= c0[:, None] + rng - 1)
+    return in_r & in_c
+
+
+def draft_block_mask(q_w, k_w, nheads, q_temporal, local, topk):
+    """Keep-mask selection of lcsa/reference.py:37-64 (= upstream generate_draft_block_mask).
+
+    Window-mean pool (bf16 result) -> per-head scores / sqrt(d) (bf16) -> -inf outside the
+    local mask tiled over time rows -> softmax over keys (bf16) -> per (head, query time
+    row) the (k+1)-th largest probability of the flattened slab is the threshold; keep is
+    strictly greater.  Returns [H, NQ, NK] bool.
+    """
+    NQ, _, C = q_w.shape
+    NK = k_w.shape[0]
+    d = C // nheads
+    aq = q_w.mean(dim=1).reshape(NQ, nheads, d).permute(1, 0, 2)  # [H, NQ, d] bf16
+    ak = k_w.mean(dim=1).reshape(NK, nheads, d).permute(1, 0, 2)
+    scores = torch.matmul(aq, ak.transpose(1, 2)) / math.sqrt(d)
+    sq, sk = local.shape
+    lm = local.repeat(NQ // sq, NK // sk)
+    scores = scores.masked_fill(~lm[None], float("-inf"))
+    prob = torch.softmax(scores, dim=-1)
+    per_row = NQ // q_temporal
+    flat = prob.reshape(nheads * q_temporal, per_row * NK)
+    k = min(flat.shape[1] - 1, topk)
+    thr = torch.topk(flat, k=k + 1, dim=1).values[:, -1:]
+    return (flat > thr).reshape(nheads, NQ, NK)
+
+
+def causal_topk_mask(q_w, k_w, nheads, per_row, ratio):
+    """Benchmark keep rule (synthetic causal rule of the attention configuration).
+
+    Query block i sits in time row (NK-NQ)/per_row + i//per_row, key block j in row
+    j//per_row.  Keep the query's own time row, plus the floor(ratio*#past) past blocks
+    with the largest mean-pooled q.k score (ties -> lower index), never a future row.
+    """
+    NQ, _, C = q_w.shape
+    NK = k_w.shape[0]
+    d = C // nheads
+    aq = q_w.float().mean(dim=1).reshape(NQ, nheads, d).permute(1, 0, 2)
+    ak = k_w.float().mean(dim=1).reshape(NK, nheads, d).permute(1, 0, 2)
+    sc = torch.matmul(aq, ak.transpose(1, 2))  # [H, NQ, NK]
+    keep = torch.zeros(nheads, NQ, NK, dtype=torch.bool)
+    cache_rows = (NK - NQ) // per_row
+    for i in range(NQ):
+        row = cache_rows + i // per_row
+        keep[:, i, row * per_row:(row + 1) * per_row] = True
+        npast = row * per_row
+        nsel = int(math.floor(ratio * npast))
+        if nsel > 0:
+            for h in range(nheads):
+                order = sorted(range(npast), key=lambda j: (-float(sc[h, i, j]), j))
+                keep[h, i, order[:nsel]] = True
+    return keep
+
+
+def build_csr(keep):
+    """build_csr (lcsa/triton_lcsa.py:64-71) without truncation: kept block ids ascending,
+    then unkept ids ascending (the stable descending argsort order); row length NK."""
+    H, NQ, NK = keep.shape
+    cnt = keep.sum(-1).to(torch.int32)
+    order = torch.argsort(keep.to(torch.int8), dim=-1, descending=True, stable=True)
+    return order.to(torch.int32), cnt
+
+
+def sparse_attention(q_w, k_w, v_w, keep):
+    """sparse_attention_ref (lcsa/reference.py:67-88): fp32, per (head, query block).
+
+    q_w [NQ, S, H*d], k_w/v_w [NK, S, H*d]; keep [H, NQ, NK].  Rows whose selection is
+    empty return 0 (the kernel's convention, triton_lcsa.py:57-59).
+    """
+    NQ, S, C = q_w.shape
+    H = keep.shape[0]
+    d = C // H
+    scale = 1.0 / math.sqrt(d)
+    q = q_w.float().reshape(NQ, S, H, d).permute(2, 0, 1, 3)
+    k = k_w.float().reshape(-1, S, H, d).permute(2, 0, 1, 3)
+    v = v_w.float().reshape(-1, S, H, d).permute(2, 0, 1, 3)
+    out = torch.zeros_like(q)
+    for h in range(H):
+        for i in range(NQ):
+            sel = keep[h, i].nonzero(as_tuple=True)[0]
+            if sel.numel() == 0:
+                continue
+            kk = k[h, sel].reshape(-1, d)
+            vv = v[h, sel].reshape(-1, d)
+            p = torch.softmax(q[h, i] @ kk.t() * scale, dim=-1)
+            out[h, i] = p @ vv
+    return out.permute(1, 2, 0, 3).reshape(NQ, S, C)
+
+
+def dense_attention(q, k, v, nheads):
+    """Plain softmax attention, q [Lq, H*d], k/v [Lk, H*d] (cross-attention; fp32)."""
+    Lq, C = q.shape
+    d = C // nheads
+    qh = q.float().reshape(Lq, nheads, d).transpose(0, 1)
+    kh = k.float().reshape(-1, nheads, d).transpose(0, 1)
+    vh = v.float().reshape(-1, nheads, d).transpose(0, 1)
+    p = torch.softmax(qh @ kh.transpose(1, 2) / math.sqrt(d), dim=-1)
+    return (p @ vh).transpose(0, 1).reshape(Lq, C)
+
+
+# ----------------------------------------------------------------------------- inputs
+def fp8_outlier_activations(M, K, gen, frac=0.01, mult=20.0):
+    """Benchmark GEMM activations: N(0,1) with `frac` of entries multiplied by `mult`."""
+    x = torch.randn(M, K, generator=gen)
+    mask = torch.rand(M, K, generator=gen) < frac
+    return torch.where(mask, x * mult, x).to(torch.bfloat16)

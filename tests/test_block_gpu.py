@@ -1,0 +1,152 @@
+"""Block- and model-level parity on the GPU: the DiT block as enable() wires it (every op
+on the sm_100a kernels) against the CPU oracle restatement of the same block.
+Bar: a 30-block forward within 2e-2 relative L2."""
+import pytest
+import torch
+
+from oracle import wan as OW
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def build(P_list, mode, monkeypatch, mask_rule="causal"):
+    from flashvsr_sm89_ops_b200 import wan_video_dit as W
+    from flashvsr_sm89_ops_b200.integrate import enable
+    monkeypatch.setenv("FS89_FP8_SCALE", mode)
+    W.MASK_RULE = mask_rule
+    dit = W.WanDiT(num_layers=len(P_list)).to(torch.bfloat16)
+    for blk, P in zip(dit.blocks, P_list):
+        blk.load_state_dict(OW.standin_state_dict(P), strict=True)
+    dit = dit.to(DEV)
+    enable(W.DiTPipe(dit), dit_module=W, verbose=False)
+    return W, dit
+
+
+@pytest.mark.parametrize("mode", ["token", "tensor"])
+def test_block_vs_oracle(mode, monkeypatch):
+    f, h, w, heads = 2, 16, 24, 12
+    P, x, t_mod, ctx, cache = OW.block_case(seed=1, f=f, h=h, w=w)
+    W, dit = build([P], mode, monkeypatch)
+    dit.init_cross_kv(ctx.to(DEV))
+    fr = W.grid_freqs(dit.freqs, f, h, w, f0=6).to(DEV)
+    with torch.no_grad():
+        y, ck, cv = dit.blocks[0](x.to(DEV), None, t_mod.to(DEV), fr, f, h, w, kv_len=3, is_stream=True,
+                                  pre_cache_k=cache[0].to(DEV), pre_cache_v=cache[1].to(DEV))
+    Q = OW.quantize_block(P, mode)
+    cos, sin = OW.O.freqs_cos_sin(OW.grid_freqs(f, h, w, f0=6))
+    ref, (rk, rv) = OW.block_forward(Q, x, t_mod, cos, sin, (f, h, w), OW.cross_kv(Q, ctx),
+                                     OW.causal_mask_fn(heads, 6, 0.25), heads, cache, 3)
+    assert ck.shape == rk.shape == (18, 128, 1536)  # 4 rows -> trimmed to kv_len = 3
+    assert OW.rel_l2(y.cpu(), ref) < 2e-2
+    assert OW.rel_l2(ck.cpu(), rk) < 2e-2 and OW.rel_l2(cv.cpu(), rv) < 2e-2
+
+
+def test_draft_mask_rule_block(monkeypatch):
+    """The FlashVSR selection (local window + joint top-k) on the device builder."""
+    f, h, w, heads = 2, 16, 24, 12
+    P, x, t_mod, ctx, cache = OW.block_case(seed=2, f=f, h=h, w=w)
+    W, dit = build([P], "token", monkeypatch, mask_rule="draft")
+    dit.init_cross_kv(ctx.to(DEV))
+    fr = W.grid_freqs(dit.freqs, f, h, w, f0=6).to(DEV)
+    topk = int(6 * 24 * 0.4)
+    with torch.no_grad():
+        y, _, _ = dit.blocks[0](x.to(DEV), None, t_mod.to(DEV), fr, f, h, w, topk=topk, kv_len=3,
+                                is_stream=True, pre_cache_k=cache[0].to(DEV),
+                                pre_cache_v=cache[1].to(DEV), local_range=11)
+    Q = OW.quantize_block(P, "token")
+    cos, sin = OW.O.freqs_cos_sin(OW.grid_freqs(f, h, w, f0=6))
+    local = OW.O.local_block_mask(h // 8, w // 8, 11)
+    mask_fn = lambda q_w, k_w: OW.O.draft_block_mask(q_w, k_w, heads, f // 2, local, topk)  # noqa: E731
+    ref, _ = OW.block_forward(Q, x, t_mod, cos, sin, (f, h, w), OW.cross_kv(Q, ctx), mask_fn, heads,
+                              cache, 3)
+    assert OW.rel_l2(y.cpu(), ref) < 3e-2
+
+
+def test_fused_matches_stock_branch(monkeypatch):
+    """The rebound forwards keep the stock branch (all fused flags off); both agree."""
+    f, h, w = 2, 16, 24
+    P, x, t_mod, ctx, cache = OW.block_case(seed=3, f=f, h=h, w=w)
+    W, dit = build([P], "token", monkeypatch)
+    dit.init_cross_kv(ctx.to(DEV))
+    fr = W.grid_freqs(dit.freqs, f, h, w, f0=6).to(DEV)
+    args = (x.to(DEV), None, t_mod.to(DEV), fr, f, h, w)
+    kw = dict(kv_len=3, is_stream=True, pre_cache_k=cache[0].to(DEV), pre_cache_v=cache[1].to(DEV))
+    with torch.no_grad():
+        fused, _, _ = dit.blocks[0](*args, **kw)
+        saved = (W.FUSED_ROPE_FN, W.FUSED_ADALN)
+        W.FUSED_ROPE_FN, W.FUSED_ADALN = None, None
+        try:
+            stock, _, _ = dit.blocks[0](*args, **kw)
+        finally:
+            W.FUSED_ROPE_FN, W.FUSED_ADALN = saved
+    assert OW.rel_l2(fused.cpu(), stock.cpu()) < 2e-2
+
+
+def test_30_block_forward_vs_oracle(monkeypatch):
+    f, h, w, heads, nb = 2, 16, 24, 12, 30
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(1, f * h * w, 1536, generator=g).to(torch.bfloat16)
+    t_mod = torch.randn(1, 6, 1536, generator=g).to(torch.bfloat16)
+    ctx = torch.randn(1, 512, 1536, generator=g).to(torch.bfloat16)
+    from flashvsr_sm89_ops_b200 import wan_video_dit as W
+    from flashvsr_sm89_ops_b200.integrate import enable
+    monkeypatch.setenv("FS89_FP8_SCALE", "token")
+    W.MASK_RULE = "causal"
+    dit = W.WanDiT(num_layers=nb).to(torch.bfloat16).to(DEV)
+    for i, blk in enumerate(dit.blocks):
+        P = OW.init_block_params(torch.Generator().manual_seed(100 + i))
+        blk.load_state_dict({k: v.to(DEV) for k, v in OW.standin_state_dict(P).items()})
+    enable(W.DiTPipe(dit), dit_module=W, verbose=False)
+    dit.init_cross_kv(ctx.to(DEV))
+    fr = W.grid_freqs(dit.freqs, 6, h, w, 0).to(DEV)
+    with torch.no_grad():  # start chunk (f=6): no cache
+        y, _ = dit.forward_chunk(torch.cat([x, x, x], 1).to(DEV), t_mod.to(DEV), fr, (6, h, w), None,
+                                 kv_len=3)
+    cos, sin = OW.O.freqs_cos_sin(OW.grid_freqs(6, h, w, 0))
+    ref = torch.cat([x, x, x], 1)
+    for i in range(nb):
+        Q = OW.quantize_block(OW.init_block_params(torch.Generator().manual_seed(100 + i)), "token")
+        ref, _ = OW.block_forward(Q, ref, t_mod, cos, sin, (6, h, w), OW.cross_kv(Q, ctx),
+                                  OW.causal_mask_fn(heads, 6, 0.25), heads, None, 3)
+    err = OW.rel_l2(y.cpu(), ref)
+    assert err < 2e-2, err
+
+
+def test_streaming_runner_graph_replay_equals_eager():
+    from flashvsr_sm89_ops_b200.runner import StreamingDiT
+    r = StreamingDiT(num_layers=2, height=256, width=384, device=DEV)
+    r.prime()
+    x = r.make_input(2)
+    eager = r.step(x).clone()
+    g, y = r.capture(x)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, eager)
+    x.copy_(r.make_input(2, seed=9))  # new input through the same graph
+    g.replay()
+    ref2 = r.step(x)
+    torch.cuda.synchronize()
+    assert torch.equal(y, ref2)
+    from flashvsr_sm89_ops_b200 import _lib
+    assert _lib.device_error() == 0
+
+
+def test_compat_stub_call_shape():
+    """block_sparse_attn_func with the mit-han-lab signature (compat_bsa.py:31-67)."""
+    import flashvsr_sm89_ops_b200  # noqa: F401  (installs the stand-in)
+    from block_sparse_attn import block_sparse_attn_func
+    from oracle import ops as O
+    g = torch.Generator().manual_seed(4)
+    H, d, nb = 12, 128, 6
+    q = torch.randn(nb * 128, H, d, generator=g).to(torch.bfloat16)
+    k = torch.randn(nb * 128, H, d, generator=g).to(torch.bfloat16)
+    v = torch.randn(nb * 128, H, d, generator=g).to(torch.bfloat16)
+    keep = torch.rand(1, H, nb, nb, generator=g) < 0.5
+    out = block_sparse_attn_func(q.to(DEV), k.to(DEV), v.to(DEV), None, None, None, None,
+                                 keep.to(DEV), nb * 128, nb * 128)
+    ref = O.sparse_attention(q.view(nb, 128, H * d), k.view(nb, 128, H * d), v.view(nb, 128, H * d), keep[0])
+    assert torch.allclose(out.float().cpu().view(nb, 128, H * d), ref, atol=1e-2, rtol=1e-2)
+    with pytest.raises(NotImplementedError):
+        block_sparse_attn_func(q.to(DEV), k.to(DEV), v.to(DEV), None, None, None, None, keep.to(DEV),
+                               1, 1, is_causal=True)

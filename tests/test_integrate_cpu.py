@@ -1,0 +1,89 @@
+"""enable() wiring on CPU (no kernels run): flag handling, FP8 conversion counts, the
+upstream-drift guard, idempotent re-enable, and the fused-QKV weight packing."""
+import types
+
+import pytest
+import torch
+
+from flashvsr_sm89_ops_b200 import wan_video_dit as W
+from flashvsr_sm89_ops_b200.fp8_ffn import FP8FFN
+from flashvsr_sm89_ops_b200.fp8_linear import FP8Linear
+from flashvsr_sm89_ops_b200.integrate import _check_dit_structure, _qkv_pack, _row_maps, enable
+
+
+def small_pipe(layers=2, dim=256, heads=2, ffn=512):
+    dit = W.WanDiT(num_layers=layers, dim=dim, num_heads=heads, ffn_dim=ffn).to(torch.bfloat16)
+    dit.init_random(seed=0)
+    return W.DiTPipe(dit)
+
+
+def test_enable_converts_and_patches(monkeypatch):
+    monkeypatch.setenv("FS89_FP8_SCALE", "token")
+    pipe = small_pipe()
+    applied = enable(pipe, dit_module=W, verbose=False)
+    assert applied["fp8_linears"] == 2 * 10 and applied["fp8_ffn_blocks"] == 2
+    assert applied["fused_rope"] and applied["fused_adaln"] and applied["lcsa_backend"] == "b200"
+    blk = pipe.dit.blocks[0]
+    assert isinstance(blk.self_attn.q, FP8Linear) and isinstance(blk.ffn, FP8FFN)
+    assert W._FS89_PATCHED and W.FUSED_ROPE_FN is not None
+    again = enable(pipe, dit_module=W, verbose=False)  # idempotent
+    assert again["fp8_linears"] == 0 and again["fp8_ffn_blocks"] == 0
+
+
+def test_flags_turn_parts_off(monkeypatch):
+    monkeypatch.setenv("FS89_FP8", "")
+    monkeypatch.setenv("FS89_FUSED_ROPE", "0")
+    monkeypatch.setenv("FS89_FUSED_ADALN", "0")
+    pipe = small_pipe(layers=1)
+    applied = enable(pipe, dit_module=W, verbose=False)
+    assert "fp8_linears" not in applied
+    assert W.FUSED_ROPE_FN is None and W.FUSED_ADALN is None
+    monkeypatch.setenv("FS89_FUSED_ROPE", "1")
+    monkeypatch.setenv("FS89_FUSED_ADALN", "1")
+    enable(pipe, dit_module=W, verbose=False)
+    assert W.FUSED_ROPE_FN is not None
+
+
+def test_structure_guard():
+    bad = types.ModuleType("bad_dit")
+    with pytest.raises(RuntimeError, match="no SelfAttention"):
+        _check_dit_structure(bad)
+
+    class SelfAttention:
+        def forward(self, x, freqs):
+            pass
+
+    bad.SelfAttention = SelfAttention
+    with pytest.raises(RuntimeError, match="lacks args"):
+        _check_dit_structure(bad)
+
+
+def test_qkv_pack_is_exact_concatenation(monkeypatch):
+    for mode in ("tensor", "token"):
+        monkeypatch.setenv("FS89_FP8_SCALE", mode)
+        pipe = small_pipe(layers=1)
+        enable(pipe, dit_module=W, verbose=False)
+        att = pipe.dit.blocks[0].self_attn
+        _, Wq, S, Bv, m = _qkv_pack(att)
+        D = att.q.out_features
+        assert m == mode and Wq.shape == (3 * D, D) and S.shape == (3 * D,)
+        for i, lin in enumerate((att.q, att.k, att.v)):
+            assert torch.equal(Wq[i * D:(i + 1) * D].view(torch.uint8), lin.weight.view(torch.uint8))
+            s = lin.w_scale.expand(D) if lin.w_scale.numel() == 1 else lin.w_scale
+            assert torch.equal(S[i * D:(i + 1) * D], s)
+
+
+def test_row_maps_invert_window_partition():
+    from oracle import ops as O
+    r2w, w2r = _row_maps(2, 16, 24, "cpu")
+    idx = torch.arange(2 * 16 * 24).view(1, 2, 16, 24, 1)
+    assert torch.equal(O.window_partition(idx).reshape(-1).int(), w2r)
+    assert torch.equal(r2w[w2r.long()], torch.arange(2 * 16 * 24, dtype=torch.int32))
+
+
+def test_forward_refuses_cpu(monkeypatch):
+    monkeypatch.setenv("FS89_FP8_SCALE", "token")
+    lin = torch.nn.Linear(32, 16).to(torch.bfloat16)
+    fl = FP8Linear(lin)
+    with pytest.raises(ValueError, match="CUDA"):
+        fl(torch.zeros(2, 32, dtype=torch.bfloat16))

@@ -1,0 +1,318 @@
+"""Op-level parity of the sm_100a kernels (through the C ABI) against the CPU oracle.
+
+Bars: FP8 codes and scales bit-exact; gate-add bitwise;
+LN-mod / RMS-RoPE within 1 bf16 ulp on a tiny fraction of elements; GEMM / FFN /
+attention within 1e-2 max relative error (attention: the reference test's
+atol = rtol = 1e-2, lcsa/test_correctness.py:59).
+"""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import ops as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def gen(seed=0):
+    return torch.Generator().manual_seed(seed)
+
+
+def bf16_ulp(t):
+    """bf16 unit in the last place at |t| (8 significant bits)."""
+    mag = t.float().abs().clamp(min=2.0 ** -126)
+    return torch.pow(2.0, torch.floor(torch.log2(mag)) - 7)
+
+
+def within_ulps(out, ref, operand_mag, n=1.0):
+    """|out-ref| <= n ulp of the output + n ulp of the operand magnitude feeding the last
+    add/rotation (an fp32-last-bit difference upstream of a cancelling add moves the
+    bf16 result by one ulp of the operands, not of the small result)."""
+    out = out.float().cpu()
+    ref = ref.float().cpu()
+    tol = n * (bf16_ulp(torch.maximum(out.abs(), ref.abs())) + bf16_ulp(operand_mag.float().cpu()))
+    d = (out - ref).abs()
+    return bool((d <= tol).all()), (d > 0).float().mean().item(), d.max().item()
+
+
+def max_rel(out, ref):
+    out = out.float().cpu()
+    ref = ref.float().cpu()
+    return ((out - ref).abs().max() / ref.abs().max().clamp(min=1e-12)).item()
+
+
+# ----------------------------------------------------------------------------- quant
+@pytest.mark.parametrize("M,K", [(257, 1536), (64, 8960), (33, 24), (1, 1536), (128, 4608)])
+@pytest.mark.parametrize("mode", ["tensor", "token"])
+def test_quantize_fp8_bitexact(M, K, mode):
+    from flashvsr_sm89_ops_b200 import quantize_fp8
+    x = O.fp8_outlier_activations(M, K, gen(M + K))
+    q, s = quantize_fp8(x.to(DEV), mode)
+    qr, sr = O.quantize_fp8(x, mode)
+    assert torch.equal(q.view(torch.uint8).cpu(), qr.view(torch.uint8))
+    assert torch.equal(s.cpu(), sr.float())
+
+
+def test_quantize_fp8_tensor_ragged_and_empty():
+    from flashvsr_sm89_ops_b200 import quantize_fp8
+    x = torch.randn(7, 13, generator=gen(3)).to(torch.bfloat16)
+    q, s = quantize_fp8(x.to(DEV), "tensor")
+    qr, sr = O.quantize_fp8(x, "tensor")
+    assert torch.equal(q.view(torch.uint8).cpu(), qr.view(torch.uint8))
+    assert torch.equal(s.cpu(), sr)
+    q0, s0 = quantize_fp8(torch.empty(0, 1536, dtype=torch.bfloat16, device=DEV))
+    assert q0.shape == (0, 1536) and s0.item() == 0.0
+    z = torch.zeros(4, 64, dtype=torch.bfloat16, device=DEV)
+    qz, sz = quantize_fp8(z, "token")
+    assert qz.view(torch.uint8).eq(0).all() and sz.eq(0).all()
+
+
+@pytest.mark.parametrize("mode", ["tensor", "token"])
+def test_gelu_quant_matches_gpu_eager_bitexact(mode):
+    from flashvsr_sm89_ops_b200 import quantize_fp8
+    from flashvsr_sm89_ops_b200.fp8_quant import fused_gelu_quant_fp8
+    h = (torch.randn(96, 8960, generator=gen(5)) * 3).to(torch.bfloat16).to(DEV)
+    q, s = fused_gelu_quant_fp8(h, mode)
+    g = F.gelu(h, approximate="tanh")  # torch eager on the same GPU
+    qe, se = quantize_fp8(g, mode)
+    assert torch.equal(s, se)
+    neq = (q.view(torch.uint8) != qe.view(torch.uint8)).sum().item()
+    assert neq == 0, f"{neq} codes differ from quantize_fp8(F.gelu(h)) on the GPU"
+    # against the CPU oracle: CPU and CUDA tanh may differ by an fp32 ulp (rare bf16 flips)
+    qr, sr = O.gelu_quant_fp8(h.cpu(), mode)
+    d = (q.view(torch.uint8).cpu().to(torch.int16) - qr.view(torch.uint8).to(torch.int16)).abs()
+    assert d.max().item() <= 1 and (d > 0).float().mean().item() < 1e-3
+
+
+# ----------------------------------------------------------------------------- AdaLN
+def test_gate_add_bitwise():
+    from flashvsr_sm89_ops_b200 import fused_gate_add
+    B, L, D = 2, 528, 1536
+    x = torch.randn(B, L, D, generator=gen(1)).to(torch.bfloat16)
+    r = torch.randn(B, L, D, generator=gen(2)).to(torch.bfloat16)
+    g = torch.randn(B, 1, D, generator=gen(3)).to(torch.bfloat16)
+    out = fused_gate_add(x.to(DEV), g.to(DEV), r.to(DEV)).cpu()
+    assert torch.equal(out, O.gate_add(x, g, r))
+    assert torch.equal(out, x + g * r)  # eager bf16 (fused_adaln.py:8-12 "bitwise")
+
+
+@pytest.mark.parametrize("B,L,D", [(1, 16896, 1536), (2, 37, 256)])
+def test_ln_modulate(B, L, D):
+    from flashvsr_sm89_ops_b200 import fused_ln_modulate, quantize_fp8
+    x = (torch.randn(B, L, D, generator=gen(4)) * 2 + 0.5).to(torch.bfloat16)
+    mod = torch.randn(B, 6, D, generator=gen(5)).to(torch.bfloat16)
+    shift, scale = mod[:, 0:1].contiguous(), mod[:, 1:2].contiguous()
+    out, q8, qs = fused_ln_modulate(x.to(DEV), scale.to(DEV), shift.to(DEV), emit_fp8=True)
+    ref = O.ln_modulate(x, scale, shift)
+    # operand of the final add: bf16(xn * bf16(1 + scale))
+    xf = x.float()
+    xn = (xf - xf.mean(-1, keepdim=True)) / torch.sqrt(xf.var(-1, unbiased=False, keepdim=True) + 1e-6)
+    y1 = xn * (1 + scale.float())
+    ok, frac, dmax = within_ulps(out, ref, y1)
+    assert ok and frac < 1e-3, (frac, dmax)
+    qq, ss = quantize_fp8(out.reshape(-1, D), "token")
+    assert torch.equal(q8.view(torch.uint8), qq.view(torch.uint8)) and torch.equal(qs, ss)
+
+
+def test_layer_norm_affine():
+    from flashvsr_sm89_ops_b200.fused_adaln import layer_norm
+    x = torch.randn(1, 4224, 1536, generator=gen(6)).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(1536, generator=gen(7))).to(torch.bfloat16)
+    b = (0.1 * torch.randn(1536, generator=gen(8))).to(torch.bfloat16)
+    out = layer_norm(x.to(DEV), w.to(DEV), b.to(DEV))
+    xf = x.float()
+    xn = (xf - xf.mean(-1, keepdim=True)) / torch.sqrt(xf.var(-1, unbiased=False, keepdim=True) + 1e-6)
+    ok, frac, dmax = within_ulps(out, O.layer_norm(x, w, b), xn * w.float())
+    assert ok and frac < 1e-2, (frac, dmax)
+
+
+# ----------------------------------------------------------------------------- RMS+RoPE
+def _wan_freqs(L):
+    from oracle.wan import grid_freqs
+    f, h, w = 4, 48, 88
+    assert f * h * w == L
+    return grid_freqs(f, h, w)
+
+
+@pytest.mark.parametrize("rope", [True, False])
+def test_rms_rope(rope):
+    from flashvsr_sm89_ops_b200 import fused_rms_rope
+    L, D = 16896, 1536
+    x = torch.randn(1, L, D, generator=gen(9)).to(torch.bfloat16)
+    wgt = (1 + 0.1 * torch.randn(D, generator=gen(10))).to(torch.bfloat16)
+    freqs = _wan_freqs(L)
+    out = fused_rms_rope(x.to(DEV), wgt.to(DEV), freqs.to(DEV), eps=1e-6, rope=rope)
+    cos, sin = O.freqs_cos_sin(freqs)
+    ref = O.rms_rope(x, wgt, cos, sin, eps=1e-6, rope=rope)
+    # operands of the rotation: the normalised pair (y_e, y_o); without RoPE the result itself
+    y = O.rms_rope(x, wgt, rope=False).float()
+    pair = y.view(1, L, D // 2, 2).abs().amax(-1, keepdim=True).expand(1, L, D // 2, 2).reshape(1, L, D)
+    ok, frac, dmax = within_ulps(out, ref, pair if rope else ref.float())
+    assert ok and frac < 1e-3, (frac, dmax)
+
+
+# ----------------------------------------------------------------------------- layout
+def test_window_partition_roundtrip():
+    from flashvsr_sm89_ops_b200.lcsa import window_partition, window_reverse
+    f, h, w, C = 4, 48, 88, 1536
+    x = torch.randn(1, f * h * w, C, generator=gen(11)).to(torch.bfloat16)
+    xw = window_partition(x.to(DEV), (f, h, w))
+    ref = O.window_partition(x.view(1, f, h, w, C)).reshape(-1, C)
+    assert torch.equal(xw.cpu(), ref)
+    back = window_reverse(xw, (f, h, w))
+    assert torch.equal(back.cpu(), x.view(-1, C))
+
+
+def test_mask_to_csr_exact():
+    from flashvsr_sm89_ops_b200.lcsa import build_csr
+    keep = torch.rand(12, 66, 264, generator=gen(12)) < 0.3
+    keep[0, 0] = False
+    keep[1, 1] = True
+    sel, cnt, maxk = build_csr(keep.to(DEV))
+    sr, cr = O.build_csr(keep)
+    assert maxk == 264
+    assert torch.equal(cnt.cpu(), cr) and torch.equal(sel.cpu(), sr)
+
+
+# ----------------------------------------------------------------------------- GEMM
+GEMM_CASES = [
+    (4224, 1536, 1536), (4224, 4608, 1536), (512, 8960, 1536), (512, 1536, 8960),
+    (300, 200, 80), (129, 264, 48), (1, 1536, 1536),
+]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_CASES)
+@pytest.mark.parametrize("mode", ["tensor", "token"])
+def test_fp8_gemm(M, N, K, mode):
+    from flashvsr_sm89_ops_b200 import quantize_fp8
+    from flashvsr_sm89_ops_b200.fp8_linear import fp8_mm, quantize_weight
+    g = gen(M * 7 + N + K)
+    x = O.fp8_outlier_activations(M, K, g)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g) * 0.02).to(torch.bfloat16)
+    qw, sw = quantize_weight(w.to(DEV), mode)
+    qx, sx = quantize_fp8(x.to(DEV), mode)
+    out = fp8_mm(qx, sx, qw, sw, b.to(DEV))
+    qwr, swr = O.fp8_weight(w, mode)
+    assert torch.equal(qw.view(torch.uint8).cpu(), qwr.view(torch.uint8))
+    ref = O.fp8_mm(qx.cpu(), sx.cpu(), qwr, swr, b)
+    assert max_rel(out, ref) < 1e-2
+
+
+def test_fp8_gemm_gelu_epilogue_amax():
+    from flashvsr_sm89_ops_b200 import quantize_fp8
+    from flashvsr_sm89_ops_b200 import _lib
+    from flashvsr_sm89_ops_b200.fp8_linear import fp8_mm, quantize_weight
+    M, N, K = 1000, 8960, 1536
+    g = gen(21)
+    x = O.fp8_outlier_activations(M, K, g)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g) * 0.02).to(torch.bfloat16)
+    qw, sw = quantize_weight(w.to(DEV), "token")
+    qx, sx = quantize_fp8(x.to(DEV), "token")
+    amax = torch.zeros(M, device=DEV)
+    h = fp8_mm(qx, sx, qw, sw, b.to(DEV), epilogue=_lib.FVB_EPI_GELU_AMAX, amax_out=amax)
+    plain = fp8_mm(qx, sx, qw, sw, b.to(DEV))
+    ge = F.gelu(plain, approximate="tanh")
+    assert torch.equal(h, ge), "GELU epilogue differs from eager GELU of the plain GEMM output"
+    assert torch.equal(amax, ge.float().abs().amax(dim=1))
+
+
+@pytest.mark.parametrize("mode", ["tensor", "token"])
+def test_fp8_ffn(mode):
+    from flashvsr_sm89_ops_b200.fp8_ffn import FP8FFN
+    from flashvsr_sm89_ops_b200.fp8_linear import FP8Linear
+    D, Fh, M = 1536, 8960, 777
+    g = gen(31)
+    l0 = torch.nn.Linear(D, Fh)
+    l2 = torch.nn.Linear(Fh, D)
+    with torch.no_grad():
+        for lin in (l0, l2):
+            lin.weight.copy_(torch.randn(lin.weight.shape, generator=g) * 0.02)
+            lin.bias.copy_(torch.randn(lin.bias.shape, generator=g) * 0.02)
+    l0 = l0.to(torch.bfloat16)
+    l2 = l2.to(torch.bfloat16)
+    import copy
+    ffn = FP8FFN(FP8Linear(copy.deepcopy(l0).to(DEV), mode), FP8Linear(copy.deepcopy(l2).to(DEV), mode))
+    x = torch.randn(1, M, D, generator=g).to(torch.bfloat16)
+    out = ffn(x.to(DEV))
+    q0, s0 = O.fp8_weight(l0.weight.detach(), mode)
+    q2, s2 = O.fp8_weight(l2.weight.detach(), mode)
+    ref = O.fp8_ffn(x, q0, s0, l0.bias.detach(), q2, s2, l2.bias.detach(), mode)
+    assert max_rel(out, ref) < 1e-2
+
+
+# ----------------------------------------------------------------------------- attention
+ATTN_CASES = [(16, 24, 0, 0.4), (32, 48, 0, 0.3), (48, 88, 198, 0.46)]  # lcsa/test_correctness.py:46-50
+
+
+@pytest.mark.parametrize("h_lat,w_lat,nk_extra,ratio", ATTN_CASES)
+def test_block_sparse_attention(h_lat, w_lat, nk_extra, ratio):
+    from flashvsr_sm89_ops_b200.lcsa import block_sparse_attention
+    H, Dh, S, f = 12, 128, 128, 2
+    g = gen(0)
+    L = f * h_lat * w_lat
+    bh, bw = h_lat // 8, w_lat // 8
+    Nq = (f // 2) * bh * bw
+    Nk = Nq + nk_extra
+    q = torch.randn(1, L, H * Dh, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, Nk * S, H * Dh, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, Nk * S, H * Dh, generator=g).to(torch.bfloat16)
+    q_w = O.window_partition(q.view(1, f, h_lat, w_lat, H * Dh))
+    local = O.local_block_mask(bh, bw, 11)
+    keep = O.draft_block_mask(q_w, k.view(Nk, S, H * Dh), H, f // 2, local, int(Nq * Nk * ratio))
+    keep[0, 0] = False  # an empty row must come back as zeros
+    out = block_sparse_attention(q_w.reshape(1, -1, H * Dh).to(DEV), k.to(DEV), v.to(DEV), keep.to(DEV))
+    ref = O.sparse_attention(q_w, k.view(Nk, S, H * Dh), v.view(Nk, S, H * Dh), keep).reshape(1, -1, H * Dh)
+    assert torch.allclose(out.float().cpu(), ref, atol=1e-2, rtol=1e-2), \
+        (out.float().cpu() - ref).abs().max().item()
+    assert out[0, :S, :Dh].abs().max().item() == 0.0
+
+
+def test_dense_attention_cross():
+    from flashvsr_sm89_ops_b200.lcsa import dense_attention
+    H, Dh = 12, 128
+    g = gen(41)
+    q = torch.randn(1000, H * Dh, generator=g).to(torch.bfloat16)
+    k = torch.randn(512, H * Dh, generator=g).to(torch.bfloat16)
+    v = torch.randn(512, H * Dh, generator=g).to(torch.bfloat16)
+    out = dense_attention(q.to(DEV), k.to(DEV), v.to(DEV), H)
+    ref = O.dense_attention(q, k, v, H)
+    assert torch.allclose(out.float().cpu(), ref, atol=1e-2, rtol=1e-2)
+    k2 = torch.randn(300, H * Dh, generator=g).to(torch.bfloat16)  # ragged key count
+    v2 = torch.randn(300, H * Dh, generator=g).to(torch.bfloat16)
+    out2 = dense_attention(q.to(DEV), k2.to(DEV), v2.to(DEV), H)
+    assert torch.allclose(out2.float().cpu(), O.dense_attention(q, k2, v2, H), atol=1e-2, rtol=1e-2)
+
+
+# ----------------------------------------------------------------------------- masks
+def test_draft_block_mask_device():
+    from flashvsr_sm89_ops_b200.lcsa import draft_block_mask
+    H, C, S, f, h_lat, w_lat = 12, 1536, 128, 2, 48, 88
+    g = gen(51)
+    Nq = 66
+    Nk = Nq + 198
+    q_w = torch.randn(Nq, S, C, generator=g).to(torch.bfloat16)
+    k_w = torch.randn(Nk, S, C, generator=g).to(torch.bfloat16)
+    local = O.local_block_mask(6, 11, 11)
+    topk = int(Nq * Nk * 0.46)
+    keep = draft_block_mask(q_w.to(DEV), k_w.to(DEV), H, 1, local, topk).cpu()
+    ref = O.draft_block_mask(q_w, k_w, H, 1, local, topk)
+    assert (keep == ref).float().mean().item() > 0.995
+
+
+def test_causal_topk_mask_device():
+    from flashvsr_sm89_ops_b200.lcsa import causal_topk_mask
+    H, C, S = 12, 1536, 128
+    g = gen(52)
+    Nq, Nk = 132, 132
+    q_w = torch.randn(Nq, S, C, generator=g).to(torch.bfloat16)
+    k_w = torch.randn(Nk, S, C, generator=g).to(torch.bfloat16)
+    keep = causal_topk_mask(q_w.to(DEV), k_w.to(DEV), H, 66, 0.25).cpu()
+    ref = O.causal_topk_mask(q_w, k_w, H, 66, 0.25)
+    assert keep.sum().item() == 12 * (66 * 66 + 66 * 82)  # the configuration's kept pairs
+    assert (keep == ref).float().mean().item() > 0.999
