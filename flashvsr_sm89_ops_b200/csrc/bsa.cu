@@ -19,6 +19,8 @@
 // next scores while the softmax warps work on block j.  O_j is accumulated
 // into registers (acc = acc * alpha_j + O_j), so no rescale of TMEM is ever
 // needed and every TMEM buffer has exactly one producer and one consumer.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace fvb {
@@ -337,6 +339,283 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 }  // namespace bsa
+
+// ===========================================================================
+// v2: two CTAs per SM, P and O kept in tensor memory.
+//
+// Per CTA (one query block of 128 rows, one head): Q, one K and one V tile in
+// shared memory (96 KB), 256 TMEM columns: S/P at [0,128), O at [128,256).
+//   * S_j = Q K_j^T lands in the S columns; the softmax warps read it, and write
+//     P_j = exp2(S*c - m) as packed bf16 over the first 64 of those columns
+//     (tcgen05.st); the P.V product then takes A straight from TMEM
+//     (tcgen05.mma ... [d], [a_tmem], b_desc) and accumulates into O.
+//   * O stays in TMEM for the whole key loop.  The running max used for the
+//     exponentials is only raised when a block's max exceeds it by more than
+//     2^8 (lazy rescale); then O and the row sum are rescaled in place.  At that
+//     moment every earlier MMA has completed (the S_j commit tracks them), so no
+//     extra synchronisation is needed.
+//   * A CTA runs S_j -> softmax_j -> PV_j serially; the second resident CTA fills
+//     the tensor core while this one is in softmax, and vice versa.
+// ===========================================================================
+namespace bsa2 {
+
+constexpr int kThreads = 320;
+constexpr int kSoftmaxThreads = 256;
+constexpr int kTile = 128;
+constexpr int kAtom = 128 * 128;
+constexpr int kTileBytes = 2 * kAtom;
+constexpr float kLazy = 8.0f;  // log2 units: rescale only when the max grows by > 2^8
+
+constexpr size_t kSmemBytes = (size_t)kTileBytes * 3 + 1024 /*align*/ + 3072 /*bars + xchg*/;
+
+__global__ void __launch_bounds__(kThreads, 2)
+    bsa_fwd_v2_kernel(const __grid_constant__ CUtensorMap tmQ,
+                      const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const bsa::Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  uint8_t* sQ = base;
+  uint8_t* sK = sQ + kTileBytes;
+  uint8_t* sV = sK + kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kTileBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 2;
+  uint64_t* v_full = bars + 3;
+  uint64_t* v_empty = bars + 4;
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* pv_done = bars + 7;
+  uint64_t* x_bar = bars + 8;  // [2]
+  uint64_t* l_bar = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  float* xmax = reinterpret_cast<float*>(bars + 16);  // [2 parity][2 halves][128]
+  float* xl = xmax + 2 * 2 * 128;                     // [2 halves][128]
+
+  const int warp = warp_id_uniform();
+  const int lane = threadIdx.x & 31;
+  const int qb = blockIdx.x;
+  const int h = blockIdx.y;
+  const int64_t rowid = (int64_t)h * args.NQ + qb;
+  const int cnt = __ldg(args.cnt + rowid);
+  const int32_t* sel = args.sel + rowid * args.sel_stride;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(k_full, 1);
+    mbar_init(k_empty, 1);
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 8);
+    mbar_init(pv_done, 1);
+    mbar_init(&x_bar[0], kSoftmaxThreads);
+    mbar_init(&x_bar[1], kSoftmaxThreads);
+    mbar_init(l_bar, kSoftmaxThreads);
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem;         // S / P
+  const uint32_t tO = tmem + 128;   // O
+  const int col_q = h * kTile;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && cnt > 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_2d(sQ, &tmQ, q_full, col_q, qb * kTile);
+      tma_load_2d(sQ + kAtom, &tmQ, q_full, col_q + 64, qb * kTile);
+      for (int j = 0; j < cnt; ++j) {
+        const uint32_t ph = (uint32_t)j & 1u;
+        const int krow = __ldg(sel + j) * kTile;
+        if (!mbar_wait(k_empty, ph ^ 1u, 0x301u)) break;
+        mbar_arrive_expect_tx(k_full, kTileBytes);
+        tma_load_2d(sK, &tmK, k_full, col_q, krow);
+        tma_load_2d(sK + kAtom, &tmK, k_full, col_q + 64, krow);
+        if (!mbar_wait(v_empty, ph ^ 1u, 0x302u)) break;
+        mbar_arrive_expect_tx(v_full, kTileBytes);
+        tma_load_2d(sV, &tmV, v_full, col_q, krow);
+        tma_load_2d(sV + kAtom, &tmV, v_full, col_q + 64, krow);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && cnt > 0) {
+      constexpr uint32_t idesc_s = make_idesc(1 /*bf16*/, 1 /*bf16*/, 0, 0, 128, 128);
+      constexpr uint32_t idesc_o = make_idesc(1, 1, 0 /*P K-major*/, 1 /*V MN-major*/, 128, 128);
+      const uint32_t q0 = smem_u32(sQ);
+      const uint32_t k0 = smem_u32(sK);
+      const uint32_t v0 = smem_u32(sV);
+      bool ok = mbar_wait(q_full, 0, 0x303u);
+      for (int j = 0; j < cnt && ok; ++j) {
+        const uint32_t ph = (uint32_t)j & 1u;
+        if (!mbar_wait(k_full, ph, 0x304u)) break;
+        // S/P columns are reused: P_{j-1} must have been consumed by PV_{j-1}
+        if (j > 0 && !mbar_wait(pv_done, ph ^ 1u, 0x305u)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * kAtom + (kk & 3) * 32);
+          mma_f16(tS, smem_desc_sw128(q0 + off, 16, 1024), smem_desc_sw128(k0 + off, 16, 1024),
+                  idesc_s, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full);
+        tc_commit(k_empty);
+        if (!mbar_wait(p_full, ph, 0x306u)) break;
+        if (!mbar_wait(v_full, ph, 0x307u)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          // keys [16kk, 16kk+16): P of half g sits in columns [64g, 64g+32) of the S region
+          const uint32_t pcol = (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
+          mma_f16_ts(tO, tS + pcol,
+                     smem_desc_sw128(v0 + (uint32_t)(kk * 16 * 128), (uint32_t)kAtom, 1024),
+                     idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(pv_done);
+        tc_commit(v_empty);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int g = warp >> 2;         // key / value column half
+    const int qr = warp & 3;         // TMEM lane quarter
+    const int row = qr * 32 + lane;  // query row within the block
+    const uint32_t lane_addr = (uint32_t)(qr * 32) << 16;
+    const float c = args.scale_log2;
+    float m_used = -INFINITY;  // max (log2 domain) the exponentials are taken against
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < cnt; ++j) {
+      const uint32_t ph = (uint32_t)j & 1u;
+      if (!mbar_wait(s_full, ph, 0x308u)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s[64];
+      tmem_ld_32x32b_x32(tS + lane_addr + (uint32_t)(g * 64), s);
+      tmem_ld_32x32b_x32(tS + lane_addr + (uint32_t)(g * 64 + 32), s + 32);
+      tmem_ld_wait();
+      const int key0 = __ldg(sel + j) * kTile + g * 64;
+      if (key0 + 64 > args.kv_len) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (key0 + i >= args.kv_len) s[i] = __float_as_uint(-INFINITY);
+      }
+      float pm = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) pm = fmaxf(pm, __uint_as_float(s[i]));
+      float* xm = xmax + (j & 1) * 256;
+      xm[g * 128 + row] = pm;
+      mbar_arrive(&x_bar[j & 1]);
+      if (!mbar_wait(&x_bar[j & 1], (uint32_t)(j >> 1) & 1u, 0x309u)) {
+        ok = false;
+        break;
+      }
+      const float mb = fmaxf(pm, xm[(g ^ 1) * 128 + row]) * c;  // block max, log2 domain
+      float alpha = 1.f;
+      const bool raise = mb > m_used + kLazy;  // also true for the first finite block
+      if (raise) {
+        alpha = (m_used == -INFINITY) ? 0.f : ex2_approx(m_used - mb);
+        m_used = mb;
+      }
+      // P = exp2(S*c - m_used), packed bf16 pairs, plus the partial row sum
+      const float msub = (m_used == -INFINITY) ? 0.f : m_used;
+      const uint64_t cc = f2_pack(c, c);
+      const uint64_t nm = f2_pack(-msub, -msub);
+      uint32_t pk[32];
+      uint64_t acc2 = f2_pack(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])),
+                                  cc, nm);
+        float x0, x1;
+        f2_unpack(x, x0, x1);
+        const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+        acc2 = f2_add(acc2, f2_pack(p0, p1));
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+        pk[i] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      float la, lb;
+      f2_unpack(acc2, la, lb);
+      l = l * alpha + (la + lb);
+      // P_j of this half into the first 32 columns of its own 64-column S range
+      tmem_st_32x32b_x32(tS + lane_addr + (uint32_t)(g * 64), pk);
+      if (raise && j > 0) {  // rescale O in place; every earlier MMA is complete (S_j commit)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t o[32];
+          const uint32_t oa = tO + lane_addr + (uint32_t)(g * 64 + hh * 32);
+          tmem_ld_32x32b_x32(oa, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x32(oa, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    float lt = 0.f;
+    bool have_o = false;
+    if (ok && cnt > 0 && mbar_wait(pv_done, (uint32_t)(cnt - 1) & 1u, 0x30Au)) {
+      tc_fence_after();
+      xl[g * 128 + row] = l;
+      mbar_arrive(l_bar);
+      if (mbar_wait(l_bar, 0, 0x30Bu)) {
+        lt = l + xl[(g ^ 1) * 128 + row];
+        have_o = true;
+      }
+    }
+    const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+    const int qrow = qb * kTile + row;
+    const int64_t orow =
+        args.row_map ? (int64_t)__ldg(args.row_map + (qrow < args.Lq ? qrow : 0)) : (int64_t)qrow;
+    uint4* dst = reinterpret_cast<uint4*>(args.out + orow * args.ldo + col_q + g * 64);
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      uint32_t o[32];
+      if (have_o) {
+        tmem_ld_32x32b_x32(tO + lane_addr + (uint32_t)(g * 64 + hh * 32), o);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0u;
+      }
+      if (qrow < args.Lq) {
+#pragma unroll
+        for (int cch = 0; cch < 4; ++cch) {
+          float f[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(o[8 * cch + i]) * inv;
+          dst[hh * 4 + cch] = f32_to_bf16x8(f);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+}  // namespace bsa2
 }  // namespace fvb
 
 extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const int32_t* sel,
@@ -366,6 +645,11 @@ extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const in
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   static bool configured[64] = {false};
+  static int impl = -1;  // FVB_BSA_IMPL=v1 selects the first kernel generation (A/B timing)
+  if (impl < 0) {
+    const char* e = getenv("FVB_BSA_IMPL");
+    impl = (e && e[0] == 'v' && e[1] == '1') ? 1 : 2;
+  }
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -373,6 +657,10 @@ extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const in
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)bsa::kSmemBytes),
                  "bsa smem attribute");
+    FVB_CUDA_TRY(cudaFuncSetAttribute(bsa2::bsa_fwd_v2_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)bsa2::kSmemBytes),
+                 "bsa2 smem attribute");
     configured[dev] = true;
   }
   bsa::Args a;
@@ -387,7 +675,11 @@ extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const in
   a.row_map = out_row_map;
   a.out = (__nv_bfloat16*)out;
   a.ldo = (int64_t)HD;
-  bsa::bsa_fwd_kernel<<<dim3((unsigned)NQ, (unsigned)H), bsa::kThreads, bsa::kSmemBytes,
-                        (cudaStream_t)stream>>>(tq, tk, tv, a);
+  if (impl == 1)
+    bsa::bsa_fwd_kernel<<<dim3((unsigned)NQ, (unsigned)H), bsa::kThreads, bsa::kSmemBytes,
+                          (cudaStream_t)stream>>>(tq, tk, tv, a);
+  else
+    bsa2::bsa_fwd_v2_kernel<<<dim3((unsigned)NQ, (unsigned)H), bsa2::kThreads,
+                              bsa2::kSmemBytes, (cudaStream_t)stream>>>(tq, tk, tv, a);
   return check_launch("fvb_bsa_fwd");
 }

@@ -38,9 +38,12 @@ struct Args {
   float* amax_out;
 };
 
+constexpr int kStageBytes = 32 * 128;  // one epilogue warp's 32 rows x 64 bf16 columns
+constexpr int kOutBytes = EPI_WARPS * 2 * kStageBytes;
+
 template <int BN>
 constexpr size_t smem_bytes() {
-  return (size_t)STAGES * (BM + BN) * BK + 1024 /*align slack*/ + 256 /*barriers*/;
+  return (size_t)STAGES * (BM + BN) * BK + kOutBytes + 1024 /*align slack*/ + 256 /*barriers*/;
 }
 
 __device__ __forceinline__ float gelu_tanh_bf16_epi(float x) {
@@ -54,13 +57,14 @@ __device__ __forceinline__ float gelu_tanh_bf16_epi(float x) {
 template <int BN, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const Args args) {
+                    const __grid_constant__ CUtensorMap tmOut, const Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
   uint8_t* sA = base;
   uint8_t* sB = sA + STAGES * BM * BK;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * BN * BK);
+  uint8_t* sOut = sB + STAGES * BN * BK;  // epilogue staging, 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + kOutBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -85,6 +89,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmOut);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 2 * BN);
@@ -160,6 +165,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int t = 0;
+    int stage_ix = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int buf = t & 1;
       const uint32_t tph = (uint32_t)(t >> 1) & 1u;
@@ -167,57 +173,71 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int n0 = (tile % n_tiles) * BN;
       if (!mbar_wait(&tfull[buf], tph, 0x104u)) break;
       tc_fence_after();
-      const int row = m0 + q * 32 + lane;
+      const int rloc = q * 32 + lane;  // row within the tile == TMEM lane
+      const int row = m0 + rloc;
       const bool row_ok = row < args.M;
       const float sa = args.a_row ? (row_ok ? __ldg(args.sa + row) : 0.f) : __ldg(args.sa);
       const float sw0 = args.w_row ? 0.f : __ldg(args.sw);
       float tmax = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 32), r);
+      for (int c = 0; c < BN / 64; ++c) {
+        // 64 accumulator columns of this thread's row
+        uint32_t r[64];
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 64);
+        tmem_ld_32x32b_x32(taddr, r);
+        tmem_ld_32x32b_x32(taddr + 32, r + 32);
         tmem_ld_wait();
-        const int col0 = n0 + c * 32;
-        if (row_ok) {
-          __nv_bfloat16* orow = args.out + (int64_t)row * args.ldo;
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int cg = col0 + g * 8;
-            if (cg < args.N) {
-              float v[8];
-              float swv[8], bv[8];
-              if (args.w_row) {
-                const float4 s0 = __ldg(reinterpret_cast<const float4*>(args.sw + cg));
-                const float4 s1 = __ldg(reinterpret_cast<const float4*>(args.sw + cg + 4));
-                swv[0] = s0.x; swv[1] = s0.y; swv[2] = s0.z; swv[3] = s0.w;
-                swv[4] = s1.x; swv[5] = s1.y; swv[6] = s1.z; swv[7] = s1.w;
-              } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) swv[i] = sw0;
-              }
-              if (args.bias) {
-                bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(args.bias + cg)), bv);
-              } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) bv[i] = 0.f;
-              }
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                float o = __fmaf_rn(__uint_as_float(r[g * 8 + i]), sa * swv[i], bv[i]);
-                if (EPI == FVB_EPI_GELU_AMAX) {
-                  o = gelu_tanh_bf16_epi(bf16r(o));
-                  tmax = fmaxf(tmax, fabsf(o));
-                }
-                v[i] = o;
-              }
-              *reinterpret_cast<uint4*>(orow + cg) = f32_to_bf16x8(v);
-            }
-          }
+        if (c == BN / 64 - 1) {  // whole tile read: hand the accumulator back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
         }
+        const int col0 = n0 + c * 64;
+        // staging buffer of this warp for this chunk (double-buffered), 32 rows x 128 B
+        const int sb = stage_ix & 1;
+        uint8_t* stg = sOut + (size_t)((warp - 2) * 2 + sb) * kStageBytes;
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          const int cg = col0 + g * 8;
+          float v[8];
+          float swv[8], bv[8];
+          if (args.w_row && cg < args.N) {
+            const float4 s0 = __ldg(reinterpret_cast<const float4*>(args.sw + cg));
+            const float4 s1 = __ldg(reinterpret_cast<const float4*>(args.sw + cg + 4));
+            swv[0] = s0.x; swv[1] = s0.y; swv[2] = s0.z; swv[3] = s0.w;
+            swv[4] = s1.x; swv[5] = s1.y; swv[6] = s1.z; swv[7] = s1.w;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) swv[i] = sw0;
+          }
+          if (args.bias && cg < args.N) {
+            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(args.bias + cg)), bv);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) bv[i] = 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float o = __fmaf_rn(__uint_as_float(r[g * 8 + i]), sa * swv[i], bv[i]);
+            if (EPI == FVB_EPI_GELU_AMAX) {
+              o = gelu_tanh_bf16_epi(bf16r(o));
+              if (row_ok && cg < args.N) tmax = fmaxf(tmax, fabsf(o));
+            }
+            v[i] = o;
+          }
+          // 128-byte swizzle: 16-byte chunk g of row `lane` lands at chunk g ^ (lane & 7)
+          *reinterpret_cast<uint4*>(stg + lane * 128 + ((g ^ (lane & 7)) << 4)) = f32_to_bf16x8(v);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && col0 < args.N) {
+          tma_store_2d(&tmOut, stg, col0, m0 + q * 32);
+        }
+        if (lane == 0) tma_store_commit();
+        ++stage_ix;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
       if (EPI == FVB_EPI_GELU_AMAX) {
         if (args.a_row) {
           if (row_ok) atomic_max_nonneg(args.amax_out + row, tmax);
@@ -227,6 +247,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
+    if (lane == 0) tma_store_wait0();  // staging reads and global writes complete
   }
   tc_fence_before();
   __syncthreads();
@@ -245,6 +266,10 @@ static int launch(const Args& a, const void* A, const void* W, cudaStream_t st) 
   rc = make_tmap_2d(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.K, (uint64_t)a.N,
                     (uint64_t)a.K, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
+  CUtensorMap tmO;
+  rc = make_tmap_2d(&tmO, a.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)a.N, (uint64_t)a.M,
+                    (uint64_t)a.ldo * 2, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
   auto kern = fp8_gemm_kernel<BN, EPI>;
   constexpr size_t smem = smem_bytes<BN>();
   static bool configured[64] = {false};
@@ -258,21 +283,17 @@ static int launch(const Args& a, const void* A, const void* W, cudaStream_t st) 
   const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
   int grid = sm_count();
   if (tiles < grid) grid = tiles;
-  kern<<<grid, THREADS, smem, st>>>(tmA, tmB, a);
+  kern<<<grid, THREADS, smem, st>>>(tmA, tmB, tmO, a);
   return check_launch("fvb_fp8_gemm");
 }
 
-// choose the N tile: fewer partial waves wins, 256 on ties
+// choose the N tile.  A 128x256 tile moves 48 KB of operands per 4 MFLOP of MMA
+// work against 32 KB per 2 MFLOP for 128x128, and on B200 the operand feed from L2,
+// not wave quantisation, decides short-K GEMMs (measured: 8448x4608x1536 runs
+// 1.5x faster at BN=256 despite a ragged last wave).  BN=128 only for narrow N.
 static int pick_bn(int M, int N) {
-  const int sms = sm_count();
-  auto eff = [&](int bn) {
-    long tiles = (long)((M + BM - 1) / BM) * ((N + bn - 1) / bn);
-    long waves = (tiles + sms - 1) / sms;
-    // useful columns / computed columns, times wave occupancy
-    double col_eff = (double)N / (double)(((N + bn - 1) / bn) * bn);
-    return col_eff * (double)tiles / (double)(waves * sms);
-  };
-  return eff(128) > eff(256) * 1.02 ? 128 : 256;
+  (void)M;
+  return N <= 128 ? 128 : 256;
 }
 
 }  // namespace gemm

@@ -277,6 +277,67 @@ def sparse_attention(q_w, k_w, v_w, keep):
     return out.permute(1, 2, 0, 3).reshape(NQ, S, C)
 
 
+def sparse_attention_online(q_w, k_w, v_w, keep, kv_len=None, lazy=0.0):
+    """The reference kernel's evaluation order (lcsa/triton_lcsa.py:44-59): per (head, query
+    block), kept key blocks in ascending order, online softmax in the log2 domain with fp32
+    running max / sum, P rounded to bf16 before P.V (`p.to(V.dtype)`), fp32 accumulator,
+    empty rows -> 0.  Keys at index >= kv_len are masked.  Returns fp32 [NQ, S, H*d].
+
+    lazy > 0 restates the B200 kernel's variant: the max the exponentials are taken against
+    is only raised when a block's max exceeds it by more than `lazy` (log2 units), and the
+    accumulator / sum are rescaled only then (same softmax, P rounded at another scale)."""
+    NQ, S, C = q_w.shape
+    H = keep.shape[0]
+    d = C // H
+    c = (1.0 / math.sqrt(d)) * 1.4426950408889634
+    q = q_w.float().reshape(NQ, S, H, d).permute(2, 0, 1, 3)
+    k = k_w.float().reshape(-1, S, H, d).permute(2, 0, 1, 3)
+    v = v_w.float().reshape(-1, S, H, d).permute(2, 0, 1, 3)
+    out = torch.zeros_like(q)
+    for h in range(H):
+        for i in range(NQ):
+            m = torch.full((S,), float("-inf"))
+            l = torch.zeros(S)
+            acc = torch.zeros(S, d)
+            for j in keep[h, i].nonzero(as_tuple=True)[0].tolist():
+                s = (q[h, i] @ k[h, j].t()) * c
+                if kv_len is not None and (j + 1) * S > kv_len:
+                    cols = torch.arange(j * S, (j + 1) * S)
+                    s[:, cols >= kv_len] = float("-inf")
+                mb = s.max(dim=1).values
+                if lazy > 0:
+                    m_new = torch.where(mb > m + lazy, mb, m)
+                else:
+                    m_new = torch.maximum(m, mb)
+                safe = torch.where(torch.isinf(m_new), torch.zeros_like(m_new), m_new)
+                alpha = torch.where(torch.isinf(m_new), torch.ones_like(m),
+                                    torch.where(torch.isinf(m), torch.zeros_like(m), torch.exp2(m - safe)))
+                p = torch.exp2(s - safe[:, None])
+                l = l * alpha + p.sum(dim=1)
+                acc = acc * alpha[:, None] + p.to(torch.bfloat16).float() @ v[h, j]
+                m = m_new
+            out[h, i] = torch.where(l[:, None] > 0, acc / l.clamp(min=1e-30)[:, None],
+                                    torch.zeros_like(acc))
+    return out.permute(1, 2, 0, 3).reshape(NQ, S, C)
+
+
+def dense_attention_online(q, k, v, nheads, lazy=0.0):
+    """Dense attention in the kernel's order: every key block kept (cross-attention)."""
+    Lq, C = q.shape
+    Lk = k.shape[0]
+    nq, nk = -(-Lq // 128), -(-Lk // 128)
+    qp = torch.zeros(nq * 128, C, dtype=q.dtype)
+    qp[:Lq] = q
+    kp = torch.zeros(nk * 128, C, dtype=k.dtype)
+    kp[:Lk] = k
+    vp = torch.zeros(nk * 128, C, dtype=v.dtype)
+    vp[:Lk] = v
+    keep = torch.ones(nheads, nq, nk, dtype=torch.bool)
+    o = sparse_attention_online(qp.view(nq, 128, C), kp.view(nk, 128, C), vp.view(nk, 128, C),
+                                keep, kv_len=Lk, lazy=lazy)
+    return o.reshape(nq * 128, C)[:Lq]
+
+
 def dense_attention(q, k, v, nheads):
     """Plain softmax attention, q [Lq, H*d], k/v [Lk, H*d] (cross-attention; fp32)."""
     Lq, C = q.shape

@@ -99,10 +99,22 @@ def quantize_block(P, mode="token"):
 
 
 # ----------------------------------------------------------------------------- block
+# the B200 attention kernel's lazy-rescale threshold (log2 units); 0 = the reference order
+KERNEL_LAZY = 8.0
+
+
+def rmsnorm_stock(x, weight, eps=1e-6):
+    """Upstream Wan RMSNorm on bf16: bf16(x * rsqrt(mean(x^2) + eps)) * weight (a bf16 product)."""
+    xf = x.float()
+    y = (xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)).to(torch.bfloat16)
+    return y * weight.to(torch.bfloat16)
+
+
 def cross_kv(Q, context, eps=1e-6):
-    """Cached cross-attention K/V of a context (the pipeline's init_cross_kv)."""
+    """Cached cross-attention K/V of a context (the pipeline's init_cross_kv, which runs the
+    upstream norm_k, not the fused kernel)."""
     c = Q["cross"]
-    k = O.rms_rope(c["k"](context), c["norm_k"], rope=False, eps=eps)
+    k = rmsnorm_stock(c["k"](context), c["norm_k"], eps=eps)
     v = c["v"](context)
     return k.reshape(-1, k.shape[-1]), v.reshape(-1, v.shape[-1])
 
@@ -124,7 +136,7 @@ def self_attention(Q, x, cos, sin, fhw, mask_fn, nheads=12, cache=None, kv_len=N
         k_w = torch.cat([cache[0], k_w], dim=0)
         v_w = torch.cat([cache[1], v_w], dim=0)
     keep = mask_fn(q_w, k_w)
-    o_w = O.sparse_attention(q_w, k_w, v_w, keep).to(torch.bfloat16)
+    o_w = O.sparse_attention_online(q_w, k_w, v_w, keep, lazy=KERNEL_LAZY).to(torch.bfloat16)
     if kv_len is not None and k_w.shape[0] // one_len > kv_len:
         new_cache = (k_w[one_len:], v_w[one_len:])
     else:
@@ -138,7 +150,7 @@ def cross_attention(Q, x, ctx_kv, nheads=12, eps=1e-6):
     c = Q["cross"]
     B, L, D = x.shape
     q = O.rms_rope(c["q"](x), c["norm_q"], rope=False, eps=eps)
-    o = O.dense_attention(q.reshape(L, D), ctx_kv[0], ctx_kv[1], nheads).to(torch.bfloat16)
+    o = O.dense_attention_online(q.reshape(L, D), ctx_kv[0], ctx_kv[1], nheads, lazy=KERNEL_LAZY).to(torch.bfloat16)
     return c["o"](o.reshape(B, L, D))
 
 

@@ -28,13 +28,16 @@ def bf16_ulp(t):
     return torch.pow(2.0, torch.floor(torch.log2(mag)) - 7)
 
 
-def within_ulps(out, ref, operand_mag, n=1.0):
+def within_ulps(out, ref, operand_mag, n=1.0, extra=None):
     """|out-ref| <= n ulp of the output + n ulp of the operand magnitude feeding the last
     add/rotation (an fp32-last-bit difference upstream of a cancelling add moves the
-    bf16 result by one ulp of the operands, not of the small result)."""
+    bf16 result by one ulp of the operands, not of the small result) + `extra` (an
+    upstream one-ulp difference carried through a multiply)."""
     out = out.float().cpu()
     ref = ref.float().cpu()
     tol = n * (bf16_ulp(torch.maximum(out.abs(), ref.abs())) + bf16_ulp(operand_mag.float().cpu()))
+    if extra is not None:
+        tol = tol + extra.float().cpu()
     d = (out - ref).abs()
     return bool((d <= tol).all()), (d > 0).float().mean().item(), d.max().item()
 
@@ -112,7 +115,8 @@ def test_ln_modulate(B, L, D):
     xf = x.float()
     xn = (xf - xf.mean(-1, keepdim=True)) / torch.sqrt(xf.var(-1, unbiased=False, keepdim=True) + 1e-6)
     y1 = xn * (1 + scale.float())
-    ok, frac, dmax = within_ulps(out, ref, y1)
+    # xn itself may differ by one bf16 ulp (fp32 mean/var summation order), scaled by (1+s)
+    ok, frac, dmax = within_ulps(out, ref, y1, extra=(1 + scale.float()).abs() * bf16_ulp(xn))
     assert ok and frac < 1e-3, (frac, dmax)
     qq, ss = quantize_fp8(out.reshape(-1, D), "token")
     assert torch.equal(q8.view(torch.uint8), qq.view(torch.uint8)) and torch.equal(qs, ss)

@@ -76,6 +76,19 @@ def test_lcsa_oracle_matches_reference(case):
     assert torch.equal(sel[..., :g["maxk"]], g["sel"])
 
 
+@pytest.mark.parametrize("case", ["a", "b"])
+def test_online_attention_order_matches_reference(case):
+    """The kernel-order restatement (bf16 P, online softmax) agrees with the reference's fp32
+    oracle at the reference test's tolerance (lcsa/test_correctness.py:59)."""
+    g = load("lcsa.pt")[case]
+    f, h, w = g["fhw"]
+    C = g["q"].shape[-1]
+    k_w = O.window_partition(g["k"].view(1, f, h, w, C))
+    v_w = O.window_partition(g["v"].view(1, f, h, w, C))
+    on = O.sparse_attention_online(g["q_w"], k_w, v_w, g["keep"])
+    assert torch.allclose(on, g["att"].float(), atol=1e-2, rtol=1e-2)
+
+
 def test_window_reverse_roundtrip():
     x = torch.randn(1, 4, 16, 24, 8)
     xw = O.window_partition(x)
