@@ -51,7 +51,130 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--blocks", type=int, default=BLOCKS)
     p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--only", default=None, choices=sorted(ONLY_KERNELS),
+                   help="time one kernel of the step in isolation at the step's shape "
+                        "(profiling / per-kernel roofline); prints one JSON line")
     return p.parse_args()
+
+
+# kernels of one block at the step's shape, runnable in isolation (--only)
+ONLY_KERNELS = ("attention", "cross_attention", "gemm_qkv", "gemm_o", "ffn", "ln_mod_fp8",
+                "rms_rope", "gate_add", "causal_mask")
+
+
+def run_only(args, local_rank):
+    """Run one kernel class K times at the workload's shapes; report time and roofline."""
+    from flashvsr_sm89_ops_b200 import fused_gate_add, fused_ln_modulate, lcsa, quantize_fp8
+    from flashvsr_sm89_ops_b200.fp8_linear import fp8_mm
+    from flashvsr_sm89_ops_b200.fused_rms_rope import rms_rope_rows
+    from flashvsr_sm89_ops_b200.fp8_ffn import ffn_fp8
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    lat_h, lat_w = H_PX // 16, W_PX // 16
+    L = 2 * lat_h * lat_w
+    per_row = (lat_h // 8) * (lat_w // 8)
+    peaks, kind = load_peaks()
+    rnd = lambda *s: torch.randn(*s, generator=g, device=dev).to(torch.bfloat16)  # noqa: E731
+
+    def wq(n, k):
+        from flashvsr_sm89_ops_b200.fp8_linear import quantize_weight
+        return quantize_weight(0.02 * torch.randn(n, k, generator=g, device=dev).to(torch.bfloat16), "token")
+
+    x = rnd(L, D)
+    x8, sx = quantize_fp8(x, "token")
+    work, bound = None, "hbm"
+    if args.only == "attention":
+        q, k, v = rnd(L, D), rnd((KV_LEN + 1) * per_row * 128, D), rnd((KV_LEN + 1) * per_row * 128, D)
+        keep = lcsa.causal_topk_mask(q, k, HEADS, per_row, RATIO)
+        sel, cnt, _ = lcsa.build_csr(keep)
+        out = torch.empty_like(q)
+        fn = lambda: lcsa.attention_csr(q, k, v, sel, cnt, HEADS, out=out)  # noqa: E731
+        work, bound = int(keep.sum().item()) * 4 * 128 ** 3, "tensor"
+    elif args.only == "cross_attention":
+        q, k, v = rnd(L, D), rnd(CTX, D), rnd(CTX, D)
+        out = torch.empty_like(q)
+        fn = lambda: lcsa.dense_attention(q, k, v, HEADS, out=out)  # noqa: E731
+        work, bound = L * CTX * 4 * D, "tensor"
+    elif args.only in ("gemm_qkv", "gemm_o"):
+        n = 3 * D if args.only == "gemm_qkv" else D
+        w8, sw = wq(n, D)
+        out = torch.empty(L, n, dtype=torch.bfloat16, device=dev)
+        fn = lambda: fp8_mm(x8, sx, w8, sw, None, out=out)  # noqa: E731
+        work, bound = 2 * L * n * D, "tensor"
+    elif args.only == "ffn":
+        from flashvsr_sm89_ops_b200.fp8_linear import FP8Linear
+        l0 = torch.nn.Linear(D, FFN).to(torch.bfloat16).to(dev)
+        l2 = torch.nn.Linear(FFN, D).to(torch.bfloat16).to(dev)
+        f0, f2 = FP8Linear(l0, "token"), FP8Linear(l2, "token")
+        out = torch.empty(L, D, dtype=torch.bfloat16, device=dev)
+        ws = torch.empty(2 * L * FFN * 3, dtype=torch.uint8, device=dev)
+        fn = lambda: ffn_fp8(x8, sx, f0, f2, out=out, workspace=ws)  # noqa: E731
+        work, bound = 4 * L * D * FFN, "tensor"
+    elif args.only == "ln_mod_fp8":
+        sc, sh = rnd(1, 1, D), rnd(1, 1, D)
+        x3 = x.view(1, L, D)
+        fn = lambda: fused_ln_modulate(x3, sc, sh, emit_fp8=True)  # noqa: E731
+        work = L * D * (2 + 2 + 1) + L * 4
+    elif args.only == "rms_rope":
+        cos = torch.rand(L, 64, generator=g, device=dev)
+        sin = torch.rand(L, 64, generator=g, device=dev)
+        w = rnd(D)
+        out = torch.empty_like(x)
+        fn = lambda: rms_rope_rows(x, w, cos, sin, L, 1e-6, True, 128, out=out)  # noqa: E731
+        work = L * D * 4 + L * 64 * 8
+    elif args.only == "gate_add":
+        r, gt = rnd(1, L, D), rnd(1, 1, D)
+        x3 = x.view(1, L, D)
+        out = torch.empty_like(x3)
+        fn = lambda: fused_gate_add(x3, gt, r, out=out)  # noqa: E731
+        work = L * D * 6
+    elif args.only == "causal_mask":
+        q, k = rnd(L, D), rnd((KV_LEN + 1) * per_row * 128, D)
+        fn = lambda: lcsa.causal_topk_mask(q, k, HEADS, per_row, RATIO)  # noqa: E731
+        work = (L + k.shape[0]) * D * 2
+    for _ in range(max(args.warmup, 1)):
+        fn()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("fvb_only")
+    e0.record(stream)
+    for _ in range(args.steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    fp8 = args.only in ("gemm_qkv", "gemm_o", "ffn")
+    if bound == "tensor" and fp8:
+        ach, peak, unit = work / (ms / 1e3) / 1e12, measure_fp8_peak(dev), "TFLOP/s"
+        kind = "measured here: cuBLASLt FP8 8192^3 best-of-10"
+    elif bound == "tensor":
+        ach, peak, unit = work / (ms / 1e3) / 1e12, float(peaks.get("bf16_tflops", 1590.0)), "TFLOP/s"
+    else:
+        ach, peak, unit = work / (ms / 1e3) / 1e9, float(peaks.get("hbm_gbs", 6650.0)), "GB/s"
+    print(json.dumps({"only": args.only, "ms_per_launch": ms, "work_per_launch": work, "bound": bound,
+                      "achieved": ach, "peak": peak, "unit": unit, "frac": ach / peak,
+                      "peak_kind": kind}))
+
+
+def measure_fp8_peak(dev):
+    """Dense FP8 denominator: cuBLASLt torch._scaled_mm at 8192^3, best of 10 (TFLOP/s).
+    MEASURED_PEAKS.json holds bf16 only; this is the same style of measurement for FP8."""
+    n = 8192
+    a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
+    one = torch.ones(1, device=dev)
+    best = 1e9
+    for _ in range(12):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        best = min(best, e0.elapsed_time(e1))
+    return 2 * n ** 3 / (best / 1e3) / 1e12
 
 
 def load_peaks():
@@ -139,6 +262,7 @@ def cpu_block_sample(steps=1, warm=True):
     Returns (seconds per block, threads)."""
     from oracle import ops as O
     from oracle import wan
+    wan.ATTENTION = "reference"  # the reference's own fp32 attention formula
     torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(0)
     lat_h, lat_w = H_PX // 16, W_PX // 16
@@ -289,10 +413,12 @@ def run_b200(args, world, rank, local_rank):
     barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("fvb_timed")
     e0.record(stream)
     for _ in range(args.steps):
         step()
     e1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     barrier()
     clocks = sampler.stop()
@@ -373,6 +499,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, world, rank)  # rank 0 only; other ranks exit without work
+        return
+    if args.only:
+        run_only(args, local_rank)
         return
     if world > 1:
         import datetime

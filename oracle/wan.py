@@ -101,6 +101,10 @@ def quantize_block(P, mode="token"):
 # ----------------------------------------------------------------------------- block
 # the B200 attention kernel's lazy-rescale threshold (log2 units); 0 = the reference order
 KERNEL_LAZY = 8.0
+# "kernel": attention in the B200 kernel's evaluation order (parity tests of whole blocks);
+# "reference": the reference's fp32 oracle (lcsa/reference.py:67-88), used when the
+# reference's CPU path is timed (bench.py cpu_baseline / --impl reference)
+ATTENTION = "kernel"
 
 
 def rmsnorm_stock(x, weight, eps=1e-6):
@@ -136,7 +140,10 @@ def self_attention(Q, x, cos, sin, fhw, mask_fn, nheads=12, cache=None, kv_len=N
         k_w = torch.cat([cache[0], k_w], dim=0)
         v_w = torch.cat([cache[1], v_w], dim=0)
     keep = mask_fn(q_w, k_w)
-    o_w = O.sparse_attention_online(q_w, k_w, v_w, keep, lazy=KERNEL_LAZY).to(torch.bfloat16)
+    if ATTENTION == "reference":
+        o_w = O.sparse_attention(q_w, k_w, v_w, keep).to(torch.bfloat16)
+    else:
+        o_w = O.sparse_attention_online(q_w, k_w, v_w, keep, lazy=KERNEL_LAZY).to(torch.bfloat16)
     if kv_len is not None and k_w.shape[0] // one_len > kv_len:
         new_cache = (k_w[one_len:], v_w[one_len:])
     else:
@@ -150,7 +157,11 @@ def cross_attention(Q, x, ctx_kv, nheads=12, eps=1e-6):
     c = Q["cross"]
     B, L, D = x.shape
     q = O.rms_rope(c["q"](x), c["norm_q"], rope=False, eps=eps)
-    o = O.dense_attention_online(q.reshape(L, D), ctx_kv[0], ctx_kv[1], nheads, lazy=KERNEL_LAZY).to(torch.bfloat16)
+    if ATTENTION == "reference":
+        o = O.dense_attention(q.reshape(L, D), ctx_kv[0], ctx_kv[1], nheads).to(torch.bfloat16)
+    else:
+        o = O.dense_attention_online(q.reshape(L, D), ctx_kv[0], ctx_kv[1], nheads,
+                                     lazy=KERNEL_LAZY).to(torch.bfloat16)
     return c["o"](o.reshape(B, L, D))
 
 
