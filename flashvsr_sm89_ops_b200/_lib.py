@@ -43,6 +43,7 @@ _SIGS = {
     "fvb_quant_fp8_workspace_bytes": (_sz, [_i64, _i64, _int]),
     "fvb_quant_fp8": (_int, [_vp, _i64, _i64, _vp, _vp, _int, _vp, _vp]),
     "fvb_gelu_quant_fp8": (_int, [_vp, _i64, _i64, _vp, _vp, _int, _vp, _vp]),
+    "fvb_quant_fp8_tensor_noalloc": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "fvb_fp8_gemm": (_int, [_vp, _vp, _int, _vp, _vp, _int, _vp, _i64, _i64, _i64, _vp, _int, _vp, _vp]),
     "fvb_quant_fp8_with_amax": (_int, [_vp, _i64, _i64, _vp, _int, _vp, _vp, _vp]),
     "fvb_fp8_ffn_workspace_bytes": (_sz, [_i64, _i64]),

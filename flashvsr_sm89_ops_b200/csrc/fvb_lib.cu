@@ -6,3 +6,4 @@
 #include "layout.cu"
 #include "gemm_fp8.cu"
 #include "bsa.cu"
+#include "noalloc.cu"

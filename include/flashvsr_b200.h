@@ -65,6 +65,24 @@ FVB_API size_t fvb_quant_fp8_workspace_bytes(int64_t M, int64_t K, int mode);
 FVB_API int fvb_quant_fp8(const void* x, int64_t M, int64_t K, void* q, float* scale_out, int mode,
                   void* workspace, fvb_stream_t stream);
 
+/* Per-tensor FP8 quantisation that allocates nothing (no counterpart in the reference).
+ * For callers that cannot allocate device memory -- an FFI host that only passes device
+ * pointers through this C ABI, a process whose device memory belongs to another
+ * framework's pool, a loop that must not pay cudaMalloc's implicit synchronisation.
+ * Same result as fvb_quant_fp8(..., FVB_SCALE_TENSOR, workspace, ...), bit for bit, but its
+ * reduction scratch is a fixed device array inside the library (FVB_NOALLOC_QUANT_MAX_PARTIALS
+ * floats = 64 KB, held on every GPU that loads the library until the process exits).
+ *   - Limit: M*K <= FVB_NOALLOC_QUANT_MAX_PARTIALS * 65536 elements (2^30); larger inputs
+ *     are rejected with FVB_ERR_INVALID.
+ *   - It calls no cudaMalloc / cudaFree / allocating library routine.  The first call on a
+ *     device looks up the array's device address (cudaGetSymbolAddress) with that device
+ *     current; make that first call before any stream capture.
+ *   - All calls share the array, which keeps the last call's contents: calls that overlap
+ *     on the GPU (several streams or threads) race and must be ordered by the caller. */
+#define FVB_NOALLOC_QUANT_MAX_PARTIALS 16384
+FVB_API int fvb_quant_fp8_tensor_noalloc(const void* x, int64_t M, int64_t K, void* q,
+                                         float* scale_out, fvb_stream_t stream);
+
 /* ------------------------------------------------- a5: GELU(tanh) -> FP8
  * Replaces fused_gelu_quant_fp8(y2) (fp8_ffn.py:57-72; kernels :24-54):
  *   g = bf16(gelu_tanh(h))  then quantise g exactly as fvb_quant_fp8. */
