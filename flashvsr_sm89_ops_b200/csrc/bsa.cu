@@ -616,6 +616,306 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 }  // namespace bsa2
+
+// ===========================================================================
+// v3: one CTA per SM, S double-buffered in TMEM, deep K/V prefetch.
+//
+// v2 runs S_j -> softmax_j -> P.V_j serially inside a CTA and single-buffers K and
+// V, so the TMA latency of the next key window sits on the critical path (ncu: tensor
+// pipe 40% active, issue slots 31%, stalls dominated by long-scoreboard waits).  v3
+// keeps one query tile per CTA but:
+//   * two S buffers in TMEM, so S_{j+1} = Q K_{j+1}^T runs while the softmax warps
+//     work on S_j; P_j overwrites (half of) S_j's buffer as packed bf16 and the
+//     P.V MMA reads it from TMEM; O accumulates in TMEM with the lazy rescale;
+//   * a 3-stage K ring and a 2-stage V ring (160 KB) + Q (32 KB), so TMA runs two
+//     windows ahead of the tensor core;
+//   * the MMA warp issues PV_j, then (once PV_j has released the buffer) S_{j+2}.
+// TMEM: S0 [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+// ===========================================================================
+namespace bsa3 {
+
+constexpr int kThreads = 320;
+constexpr int kSoftmaxThreads = 256;
+constexpr int kTile = 128;
+constexpr int kAtom = 128 * 128;
+constexpr int kTileBytes = 2 * kAtom;
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
+constexpr float kLazy = 8.0f;
+
+constexpr size_t kSmemBytes =
+    (size_t)kTileBytes * (1 + kKStages + kVStages) + 1024 /*align*/ + 3072 /*bars + xchg*/;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bsa_fwd_v3_kernel(const __grid_constant__ CUtensorMap tmQ,
+                      const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const bsa::Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  uint8_t* sQ = base;
+  uint8_t* sK = sQ + kTileBytes;               // kKStages tiles
+  uint8_t* sV = sK + kKStages * kTileBytes;    // kVStages tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVStages * kTileBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;     // [3]
+  uint64_t* k_empty = bars + 4;    // [3]
+  uint64_t* v_full = bars + 7;     // [2]
+  uint64_t* v_empty = bars + 9;    // [2]
+  uint64_t* s_full = bars + 11;    // [2]
+  uint64_t* s_free = bars + 13;    // [2]  P of this buffer consumed by its P.V
+  uint64_t* p_full = bars + 15;    // [2]
+  uint64_t* pv_done = bars + 17;   // completes once per P.V, in order
+  uint64_t* x_bar = bars + 18;     // [2]
+  uint64_t* l_bar = bars + 20;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  float* xmax = reinterpret_cast<float*>(bars + 24);  // [2 parity][2 halves][128]
+  float* xl = xmax + 2 * 2 * 128;                     // [2 halves][128]
+
+  const int warp = warp_id_uniform();
+  const int lane = threadIdx.x & 31;
+  const int qb = blockIdx.x;
+  const int h = blockIdx.y;
+  const int64_t rowid = (int64_t)h * args.NQ + qb;
+  const int cnt = __ldg(args.cnt + rowid);
+  const int32_t* sel = args.sel + rowid * args.sel_stride;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kKStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 1);
+      mbar_init(&p_full[i], 8);
+      mbar_init(&x_bar[i], kSoftmaxThreads);
+    }
+    mbar_init(pv_done, 1);
+    mbar_init(l_bar, kSoftmaxThreads);
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tO = tmem + 256;
+  const int col_q = h * kTile;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && cnt > 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_2d(sQ, &tmQ, q_full, col_q, qb * kTile);
+      tma_load_2d(sQ + kAtom, &tmQ, q_full, col_q + 64, qb * kTile);
+      for (int j = 0; j < cnt; ++j) {
+        const int krow = __ldg(sel + j) * kTile;
+        const int ks = j % kKStages;
+        if (!mbar_wait(&k_empty[ks], (uint32_t)((j / kKStages) & 1) ^ 1u, 0x401u)) break;
+        mbar_arrive_expect_tx(&k_full[ks], kTileBytes);
+        tma_load_2d(sK + ks * kTileBytes, &tmK, &k_full[ks], col_q, krow);
+        tma_load_2d(sK + ks * kTileBytes + kAtom, &tmK, &k_full[ks], col_q + 64, krow);
+        const int vs = j & 1;
+        if (!mbar_wait(&v_empty[vs], (uint32_t)((j >> 1) & 1) ^ 1u, 0x402u)) break;
+        mbar_arrive_expect_tx(&v_full[vs], kTileBytes);
+        tma_load_2d(sV + vs * kTileBytes, &tmV, &v_full[vs], col_q, krow);
+        tma_load_2d(sV + vs * kTileBytes + kAtom, &tmV, &v_full[vs], col_q + 64, krow);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && cnt > 0) {
+      constexpr uint32_t idesc_s = make_idesc(1 /*bf16*/, 1 /*bf16*/, 0, 0, 128, 128);
+      constexpr uint32_t idesc_o = make_idesc(1, 1, 0 /*P K-major*/, 1 /*V MN-major*/, 128, 128);
+      const uint32_t q0 = smem_u32(sQ);
+      bool ok = mbar_wait(q_full, 0, 0x403u);
+      auto issue_s = [&](int j) -> bool {
+        const int ks = j % kKStages;
+        const int b = j & 1;
+        if (!mbar_wait(&k_full[ks], (uint32_t)((j / kKStages) & 1), 0x404u)) return false;
+        // buffer b last held P_{j-2}; its P.V must have consumed it
+        if (j >= 2 && !mbar_wait(&s_free[b], (uint32_t)(((j - 2) >> 1) & 1), 0x405u)) return false;
+        tc_fence_after();
+        const uint32_t k0 = smem_u32(sK + ks * kTileBytes);
+        const uint32_t d = tmem + (uint32_t)(b * 128);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * kAtom + (kk & 3) * 32);
+          mma_f16(d, smem_desc_sw128(q0 + off, 16, 1024), smem_desc_sw128(k0 + off, 16, 1024),
+                  idesc_s, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[b]);
+        tc_commit(&k_empty[ks]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && cnt > 1) ok = issue_s(1);
+      for (int j = 0; j < cnt && ok; ++j) {
+        const int b = j & 1;
+        if (!mbar_wait(&p_full[b], (uint32_t)((j >> 1) & 1), 0x406u)) break;
+        const int vs = j & 1;
+        if (!mbar_wait(&v_full[vs], (uint32_t)((j >> 1) & 1), 0x407u)) break;
+        tc_fence_after();
+        const uint32_t v0 = smem_u32(sV + vs * kTileBytes);
+        const uint32_t sb = tmem + (uint32_t)(b * 128);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          // keys [16kk, 16kk+16): P of half g sits in columns [64g, 64g+32) of the buffer
+          const uint32_t pcol = (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
+          mma_f16_ts(tO, sb + pcol,
+                     smem_desc_sw128(v0 + (uint32_t)(kk * 16 * 128), (uint32_t)kAtom, 1024),
+                     idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&v_empty[vs]);
+        tc_commit(&s_free[b]);
+        tc_commit(pv_done);
+        if (j + 2 < cnt) ok = issue_s(j + 2);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int g = warp >> 2;         // key / value column half
+    const int qr = warp & 3;         // TMEM lane quarter
+    const int row = qr * 32 + lane;  // query row within the block
+    const uint32_t lane_addr = (uint32_t)(qr * 32) << 16;
+    const float c = args.scale_log2;
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < cnt; ++j) {
+      const int b = j & 1;
+      const uint32_t tS = tmem + (uint32_t)(b * 128);
+      if (!mbar_wait(&s_full[b], (uint32_t)((j >> 1) & 1), 0x408u)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s[64];
+      tmem_ld_32x32b_x32(tS + lane_addr + (uint32_t)(g * 64), s);
+      tmem_ld_32x32b_x32(tS + lane_addr + (uint32_t)(g * 64 + 32), s + 32);
+      tmem_ld_wait();
+      const int key0 = __ldg(sel + j) * kTile + g * 64;
+      if (key0 + 64 > args.kv_len) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (key0 + i >= args.kv_len) s[i] = __float_as_uint(-INFINITY);
+      }
+      float pm = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) pm = fmaxf(pm, __uint_as_float(s[i]));
+      float* xm = xmax + (j & 1) * 256;
+      xm[g * 128 + row] = pm;
+      mbar_arrive(&x_bar[j & 1]);
+      if (!mbar_wait(&x_bar[j & 1], (uint32_t)(j >> 1) & 1u, 0x409u)) {
+        ok = false;
+        break;
+      }
+      const float mb = fmaxf(pm, xm[(g ^ 1) * 128 + row]) * c;
+      float alpha = 1.f;
+      const bool raise = mb > m_used + kLazy;
+      if (raise) {
+        alpha = (m_used == -INFINITY) ? 0.f : ex2_approx(m_used - mb);
+        m_used = mb;
+      }
+      const float msub = (m_used == -INFINITY) ? 0.f : m_used;
+      const uint64_t cc = f2_pack(c, c);
+      const uint64_t nm = f2_pack(-msub, -msub);
+      uint32_t pk[32];
+      uint64_t acc2 = f2_pack(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])),
+                                  cc, nm);
+        float x0, x1;
+        f2_unpack(x, x0, x1);
+        const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+        acc2 = f2_add(acc2, f2_pack(p0, p1));
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+        pk[i] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      float la, lb;
+      f2_unpack(acc2, la, lb);
+      l = l * alpha + (la + lb);
+      tmem_st_32x32b_x32(tS + lane_addr + (uint32_t)(g * 64), pk);
+      if (raise && j > 0) {
+        // O holds P.V of windows < j; the P.V of window j-1 may still be running
+        if (!mbar_wait(pv_done, (uint32_t)((j - 1) & 1), 0x40Au)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t o[32];
+          const uint32_t oa = tO + lane_addr + (uint32_t)(g * 64 + hh * 32);
+          tmem_ld_32x32b_x32(oa, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x32(oa, o);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+    }
+    float lt = 0.f;
+    bool have_o = false;
+    if (ok && cnt > 0 && mbar_wait(pv_done, (uint32_t)((cnt - 1) & 1), 0x40Bu)) {
+      tc_fence_after();
+      xl[g * 128 + row] = l;
+      mbar_arrive(l_bar);
+      if (mbar_wait(l_bar, 0, 0x40Cu)) {
+        lt = l + xl[(g ^ 1) * 128 + row];
+        have_o = true;
+      }
+    }
+    const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+    const int qrow = qb * kTile + row;
+    const int64_t orow =
+        args.row_map ? (int64_t)__ldg(args.row_map + (qrow < args.Lq ? qrow : 0)) : (int64_t)qrow;
+    uint4* dst = reinterpret_cast<uint4*>(args.out + orow * args.ldo + col_q + g * 64);
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      uint32_t o[32];
+      if (have_o) {
+        tmem_ld_32x32b_x32(tO + lane_addr + (uint32_t)(g * 64 + hh * 32), o);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0u;
+      }
+      if (qrow < args.Lq) {
+#pragma unroll
+        for (int cch = 0; cch < 4; ++cch) {
+          float f[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(o[8 * cch + i]) * inv;
+          dst[hh * 4 + cch] = f32_to_bf16x8(f);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace bsa3
 }  // namespace fvb
 
 extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const int32_t* sel,
@@ -645,11 +945,16 @@ extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const in
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   static bool configured[64] = {false};
-  static int impl = -1;  // FVB_BSA_IMPL=v1 selects the first kernel generation (A/B timing)
-  if (impl < 0) {
+  // Kernel generation: v3 (1 CTA/SM, deep prefetch) when the key list can be long, v2
+  // (2 CTAs/SM) for short lists such as cross-attention's 4 windows, where a co-resident
+  // CTA hides the per-CTA set-up.  FVB_BSA_IMPL=v1|v2|v3 pins one (A/B timing).
+  static int forced = -1;
+  if (forced < 0) {
     const char* e = getenv("FVB_BSA_IMPL");
-    impl = (e && e[0] == 'v' && e[1] == '1') ? 1 : 2;
+    forced = (e && e[0] == 'v' && e[1] >= '1' && e[1] <= '3') ? (e[1] - '0') : 0;
   }
+  const int64_t nk_blocks = Lk / 128;
+  const int impl = forced ? forced : (nk_blocks >= 16 ? 3 : 2);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -661,6 +966,10 @@ extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const in
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)bsa2::kSmemBytes),
                  "bsa2 smem attribute");
+    FVB_CUDA_TRY(cudaFuncSetAttribute(bsa3::bsa_fwd_v3_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)bsa3::kSmemBytes),
+                 "bsa3 smem attribute");
     configured[dev] = true;
   }
   bsa::Args a;
@@ -678,8 +987,11 @@ extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const in
   if (impl == 1)
     bsa::bsa_fwd_kernel<<<dim3((unsigned)NQ, (unsigned)H), bsa::kThreads, bsa::kSmemBytes,
                           (cudaStream_t)stream>>>(tq, tk, tv, a);
-  else
+  else if (impl == 2)
     bsa2::bsa_fwd_v2_kernel<<<dim3((unsigned)NQ, (unsigned)H), bsa2::kThreads,
                               bsa2::kSmemBytes, (cudaStream_t)stream>>>(tq, tk, tv, a);
+  else
+    bsa3::bsa_fwd_v3_kernel<<<dim3((unsigned)NQ, (unsigned)H), bsa3::kThreads,
+                              bsa3::kSmemBytes, (cudaStream_t)stream>>>(tq, tk, tv, a);
   return check_launch("fvb_bsa_fwd");
 }

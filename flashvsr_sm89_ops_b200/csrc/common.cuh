@@ -75,6 +75,20 @@ __device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float a, float b) {
   return (uint16_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
 }
 
+// x / s as the e4m3 conversion will see it, without a full IEEE divide in the common case.
+// rs = 1/s correctly rounded.  y = x * rs is within 2 fp32 ulps of the IEEE quotient
+// __fdiv_rn(x, s); their e4m3 roundings (3 mantissa bits kept, round to nearest even) can
+// only differ when y lies within a few ulps of an e4m3 rounding midpoint (fp32 mantissa low
+// 20 bits == 0x80000) or in the e4m3 subnormal range (|y| < 2^-6).  Those inputs take the
+// exact divide, so the resulting code always equals e4m3(__fdiv_rn(x, s)).
+__device__ __forceinline__ float div_for_e4m3(float x, float s, float rs) {
+  const float y = x * rs;
+  const uint32_t b = __float_as_uint(y) & 0x7fffffffu;
+  const bool near_mid = ((b & 0xFFFFFu) - 0x80000u + 8u) < 16u;
+  const bool subnormal = b < 0x3C800000u;  // 2^-6
+  return (near_mid || subnormal) ? __fdiv_rn(x, s) : y;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -4,15 +4,17 @@
 //
 //   out[m, n] = bf16(acc[m, n] * sa[m|0] * sw[n|0] + bias[n]),  acc = sum_k A[m,k] W[n,k]
 //
-// Design (one persistent CTA per SM, 192 threads, warp-specialised):
+// Design (one persistent CTA per SM, 320 threads, warp-specialised):
 //   warp 0      TMA producer: 128x128-byte A tiles and BNx128-byte W tiles
 //               (128-byte swizzle) into a 4-stage shared-memory ring
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma kind::f8f6f4
 //               (M=128, N=BN, K=32 per instruction) into a TMEM accumulator;
 //               tcgen05.commit releases ring stages and publishes finished tiles.
 //               Also allocates / frees the 2*BN TMEM columns.
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (each thread owns one
-//               output row), apply scales + bias (+ GELU / amax), store bf16.
+//   warps 2-9   epilogue, two warps per TMEM lane quarter: tcgen05.ld 32 columns
+//               at a time (each thread owns one output row, the warp pair splits the
+//               64-column chunks), scales + bias (+ GELU / amax), bf16 into a 128-byte
+//               swizzled staging buffer, TMA bulk store of 32 rows x 64 columns.
 // The accumulator is double-buffered in TMEM so the epilogue of tile t overlaps
 // the main loop of tile t+1.  Both operands are K-major ("TN"), exactly the
 // nn.Linear weight layout, so no transpose is ever materialised.
@@ -24,7 +26,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes == fp8 elements per K block
 constexpr int STAGES = 4;
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 
 struct Args {
@@ -39,7 +41,7 @@ struct Args {
 };
 
 constexpr int kStageBytes = 32 * 128;  // one epilogue warp's 32 rows x 64 bf16 columns
-constexpr int kOutBytes = EPI_WARPS * 2 * kStageBytes;
+constexpr int kOutBytes = EPI_WARPS * kStageBytes;  // one staging buffer per warp
 
 template <int BN>
 constexpr size_t smem_bytes() {
@@ -163,9 +165,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // 8 warps: two per TMEM lane quarter (warp % 4); the pair splits each tile's 64-column
+    // chunks between them (even / odd chunks), so each thread finishes half a row per tile.
+    const int q = warp & 3;               // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;     // 0: warps 2-5, 1: warps 6-9
+    uint8_t* stg = sOut + (size_t)(warp - 2) * kStageBytes;  // this warp's staging, 32 x 128 B
     int t = 0;
-    int stage_ix = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int buf = t & 1;
       const uint32_t tph = (uint32_t)(t >> 1) & 1u;
@@ -180,63 +185,63 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float sw0 = args.w_row ? 0.f : __ldg(args.sw);
       float tmax = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < BN / 64; ++c) {
-        // 64 accumulator columns of this thread's row
-        uint32_t r[64];
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 64);
-        tmem_ld_32x32b_x32(taddr, r);
-        tmem_ld_32x32b_x32(taddr + 32, r + 32);
-        tmem_ld_wait();
-        if (c == BN / 64 - 1) {  // whole tile read: hand the accumulator back to the MMA warp
+      for (int c = half; c < BN / 64; c += 2) {
+        const int col0 = n0 + c * 64;
+        // the previous TMA store from this staging buffer must have finished reading it
+        if (lane == 0) tma_store_wait_read<0>();
+        __syncwarp();
+#pragma unroll 1
+        for (int sub = 0; sub < 2; ++sub) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(
+              tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 64 + sub * 32), r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int g4 = 0; g4 < 4; ++g4) {
+            const int g = sub * 4 + g4;  // 16-byte chunk of the 128-byte staging row
+            const int cg = col0 + g * 8;
+            float v[8];
+            float swv[8], bv[8];
+            if (args.w_row && cg < args.N) {
+              const float4 s0 = __ldg(reinterpret_cast<const float4*>(args.sw + cg));
+              const float4 s1 = __ldg(reinterpret_cast<const float4*>(args.sw + cg + 4));
+              swv[0] = s0.x; swv[1] = s0.y; swv[2] = s0.z; swv[3] = s0.w;
+              swv[4] = s1.x; swv[5] = s1.y; swv[6] = s1.z; swv[7] = s1.w;
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) swv[i] = sw0;
+            }
+            if (args.bias && cg < args.N) {
+              bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(args.bias + cg)), bv);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) bv[i] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float o = __fmaf_rn(__uint_as_float(r[g4 * 8 + i]), sa * swv[i], bv[i]);
+              if (EPI == FVB_EPI_GELU_AMAX) {
+                o = gelu_tanh_bf16_epi(bf16r(o));
+                if (row_ok && cg < args.N) tmax = fmaxf(tmax, fabsf(o));
+              }
+              v[i] = o;
+            }
+            // 128-byte swizzle: 16-byte chunk g of row `lane` lands at chunk g ^ (lane & 7)
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((g ^ (lane & 7)) << 4)) =
+                f32_to_bf16x8(v);
+          }
+        }
+        if (c + 2 >= BN / 64) {  // this warp's last TMEM read of the tile
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[buf]);
         }
-        const int col0 = n0 + c * 64;
-        // staging buffer of this warp for this chunk (double-buffered), 32 rows x 128 B
-        const int sb = stage_ix & 1;
-        uint8_t* stg = sOut + (size_t)((warp - 2) * 2 + sb) * kStageBytes;
-        if (lane == 0) tma_store_wait_read<1>();
-        __syncwarp();
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          const int cg = col0 + g * 8;
-          float v[8];
-          float swv[8], bv[8];
-          if (args.w_row && cg < args.N) {
-            const float4 s0 = __ldg(reinterpret_cast<const float4*>(args.sw + cg));
-            const float4 s1 = __ldg(reinterpret_cast<const float4*>(args.sw + cg + 4));
-            swv[0] = s0.x; swv[1] = s0.y; swv[2] = s0.z; swv[3] = s0.w;
-            swv[4] = s1.x; swv[5] = s1.y; swv[6] = s1.z; swv[7] = s1.w;
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) swv[i] = sw0;
-          }
-          if (args.bias && cg < args.N) {
-            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(args.bias + cg)), bv);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) bv[i] = 0.f;
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float o = __fmaf_rn(__uint_as_float(r[g * 8 + i]), sa * swv[i], bv[i]);
-            if (EPI == FVB_EPI_GELU_AMAX) {
-              o = gelu_tanh_bf16_epi(bf16r(o));
-              if (row_ok && cg < args.N) tmax = fmaxf(tmax, fabsf(o));
-            }
-            v[i] = o;
-          }
-          // 128-byte swizzle: 16-byte chunk g of row `lane` lands at chunk g ^ (lane & 7)
-          *reinterpret_cast<uint4*>(stg + lane * 128 + ((g ^ (lane & 7)) << 4)) = f32_to_bf16x8(v);
-        }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0 && col0 < args.N) {
-          tma_store_2d(&tmOut, stg, col0, m0 + q * 32);
+        if (lane == 0) {
+          if (col0 < args.N) tma_store_2d(&tmOut, stg, col0, m0 + q * 32);
+          tma_store_commit();
         }
-        if (lane == 0) tma_store_commit();
-        ++stage_ix;
       }
       if (EPI == FVB_EPI_GELU_AMAX) {
         if (args.a_row) {

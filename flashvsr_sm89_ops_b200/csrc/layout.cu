@@ -76,23 +76,37 @@ __global__ void __launch_bounds__(256) mask_to_csr_kernel(const uint8_t* __restr
 // block pooling: mean over the 128 tokens of each window, per channel.
 // round_bf16 mirrors torch.mean on a bf16 tensor (fp32 accumulate, bf16 result).
 // ---------------------------------------------------------------------------
+// grid (windows, ceil(C / 512)), 256 threads: threadIdx.x % 64 picks one 8-channel vector of
+// this CTA's 512-channel slice, threadIdx.x / 64 one of 4 token groups (32 tokens each, 8
+// loads in flight per thread); the 4 partial sums meet in shared memory in a fixed order.
 __global__ void __launch_bounds__(256) pool_kernel(const __nv_bfloat16* __restrict__ x,
                                                     int64_t nblk, int64_t C, int round_bf16,
                                                     float* __restrict__ avg) {
+  __shared__ float part[4][64][8];
   const int64_t blk = blockIdx.x;
-  if (blk >= nblk) return;
-  const __nv_bfloat16* xb = x + blk * 128 * C;
-  for (int64_t c8 = threadIdx.x; c8 * 8 < C; c8 += blockDim.x) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int t = 0; t < 128; ++t) {
+  const int vx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  const int64_t c8 = (int64_t)blockIdx.y * 64 + vx;
+  const bool on = c8 * 8 < C;
+  const uint4* xb = reinterpret_cast<const uint4*>(x + blk * 128 * C) + c8;
+  const int64_t cv = C >> 3;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (on) {
+#pragma unroll 8
+    for (int t = ty; t < 128; t += 4) {
       float f[8];
-      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(xb + t * C) + c8), f);
+      bf16x8_to_f32(__ldg(xb + t * cv), f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] += f[i];
     }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) part[ty][vx][i] = acc[i];
+  __syncthreads();
+  if (ty == 0 && on) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      float m = __fdiv_rn(acc[i], 128.0f);
+      const float s = (part[0][vx][i] + part[1][vx][i]) + (part[2][vx][i] + part[3][vx][i]);
+      const float m = __fdiv_rn(s, 128.0f);
       avg[blk * C + c8 * 8 + i] = round_bf16 ? bf16r(m) : m;
     }
   }
@@ -338,8 +352,8 @@ int fvb_draft_block_mask(const void* q_w, const void* k_w, int64_t H, int64_t NQ
   float* aq = static_cast<float*>(workspace);
   float* ak = aq + NQ * C;
   float* prob = ak + NK * C;
-  pool_kernel<<<(unsigned)NQ, 192, 0, st>>>((const __nv_bfloat16*)q_w, NQ, C, 1, aq);
-  pool_kernel<<<(unsigned)NK, 192, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 1, ak);
+  pool_kernel<<<dim3((unsigned)NQ, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)q_w, NQ, C, 1, aq);
+  pool_kernel<<<dim3((unsigned)NK, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 1, ak);
   int rc = check_launch("fvb_draft_block_mask pool");
   if (rc) return rc;
   const size_t smem = (size_t)NK * 4;
@@ -371,8 +385,8 @@ int fvb_causal_topk_mask(const void* q_w, const void* k_w, int64_t H, int64_t NQ
   const int64_t C = H * d;
   float* aq = static_cast<float*>(workspace);
   float* ak = aq + NQ * C;
-  pool_kernel<<<(unsigned)NQ, 192, 0, st>>>((const __nv_bfloat16*)q_w, NQ, C, 0, aq);
-  pool_kernel<<<(unsigned)NK, 192, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 0, ak);
+  pool_kernel<<<dim3((unsigned)NQ, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)q_w, NQ, C, 0, aq);
+  pool_kernel<<<dim3((unsigned)NK, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 0, ak);
   int rc = check_launch("fvb_causal_topk_mask pool");
   if (rc) return rc;
   const size_t smem = (size_t)NK * 4;

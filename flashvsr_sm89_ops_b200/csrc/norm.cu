@@ -59,7 +59,9 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(
     }
   }
   const float var = __fdiv_rn(warp_sum(sq), (float)D);
-  const float den = __fsqrt_rn(var + eps);
+  // (x - mean) / sqrt(var + eps) as a product with the correctly rounded reciprocal square
+  // root: at most one fp32 ulp from the quotient, well inside the bf16 rounding that follows
+  const float rden = __frsqrt_rn(var + eps);
   const int64_t b = row / L;
   const uint4* sv = reinterpret_cast<const uint4*>(scale + b * D);
   const uint4* hv = reinterpret_cast<const uint4*>(shift + b * D);
@@ -74,7 +76,7 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(
       bf16x8_to_f32(__ldg(hv + v), h);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        float xn = bf16r(__fdiv_rn(f[j][i] - mean, den));
+        float xn = bf16r((f[j][i] - mean) * rden);
         float y = bf16r(xn * bf16r(1.0f + s[i]));
         y = bf16r(y + h[i]);
         f[j][i] = y;
@@ -86,6 +88,7 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(
   if (EMIT_FP8) {
     amax = warp_max(amax);
     const float qs = quant_scale_from_amax_n(amax);
+    const float rqs = __frcp_rn(qs);
     uint2* qv = reinterpret_cast<uint2*>(q8 + row * D);
 #pragma unroll
     for (int j = 0; j < kRowNV; ++j) {
@@ -94,10 +97,10 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(
         uint32_t w[2];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          float a0 = fminf(fmaxf(__fdiv_rn(f[j][4 * hh + 0], qs), -448.f), 448.f);
-          float a1 = fminf(fmaxf(__fdiv_rn(f[j][4 * hh + 1], qs), -448.f), 448.f);
-          float a2 = fminf(fmaxf(__fdiv_rn(f[j][4 * hh + 2], qs), -448.f), 448.f);
-          float a3 = fminf(fmaxf(__fdiv_rn(f[j][4 * hh + 3], qs), -448.f), 448.f);
+          float a0 = fminf(fmaxf(div_for_e4m3(f[j][4 * hh + 0], qs, rqs), -448.f), 448.f);
+          float a1 = fminf(fmaxf(div_for_e4m3(f[j][4 * hh + 1], qs, rqs), -448.f), 448.f);
+          float a2 = fminf(fmaxf(div_for_e4m3(f[j][4 * hh + 2], qs, rqs), -448.f), 448.f);
+          float a3 = fminf(fmaxf(div_for_e4m3(f[j][4 * hh + 3], qs, rqs), -448.f), 448.f);
           w[hh] = (uint32_t)f32x2_to_e4m3x2(a0, a1) | ((uint32_t)f32x2_to_e4m3x2(a2, a3) << 16);
         }
         qv[v] = make_uint2(w[0], w[1]);

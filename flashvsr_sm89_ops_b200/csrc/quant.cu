@@ -37,13 +37,14 @@ __device__ __forceinline__ float clamp448(float v) { return fminf(fmaxf(v, -kFp8
 
 // 8 values -> 8 e4m3 codes packed in a uint2
 __device__ __forceinline__ uint2 quant8(const float* f, float s) {
+  const float rs = __frcp_rn(s);
   uint32_t w[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    uint16_t lo = f32x2_to_e4m3x2(clamp448(__fdiv_rn(f[4 * h + 0], s)),
-                                  clamp448(__fdiv_rn(f[4 * h + 1], s)));
-    uint16_t hi = f32x2_to_e4m3x2(clamp448(__fdiv_rn(f[4 * h + 2], s)),
-                                  clamp448(__fdiv_rn(f[4 * h + 3], s)));
+    uint16_t lo = f32x2_to_e4m3x2(clamp448(div_for_e4m3(f[4 * h + 0], s, rs)),
+                                  clamp448(div_for_e4m3(f[4 * h + 1], s, rs)));
+    uint16_t hi = f32x2_to_e4m3x2(clamp448(div_for_e4m3(f[4 * h + 2], s, rs)),
+                                  clamp448(div_for_e4m3(f[4 * h + 3], s, rs)));
     w[h] = (uint32_t)lo | ((uint32_t)hi << 16);
   }
   return make_uint2(w[0], w[1]);
