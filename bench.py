@@ -475,7 +475,8 @@ def run_b200(args, world, rank, local_rank):
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": x_static.numel() * 2,
                 "d2h_bytes_per_step": y.numel() * 2},
         "gpu_launches": launches * args.steps,
-        "roofline": {"kernel": "bsa_fwd_kernel (block-sparse attention, 91,080 kept window pairs)",
+        "roofline": {"kernel": "bsa6::bsa_fwd_v6_kernel (block-sparse self-attention, 91,080 kept "
+                               "window pairs)",
                      "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} bf16 dense (burst)",
                      "traffic": traffic_from_profiles("bsa_fwd_kernel"),

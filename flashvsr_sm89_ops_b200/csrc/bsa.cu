@@ -4,21 +4,15 @@
 // (128 keys each), scores * scale, fp32 statistics, P rounded to bf16 for the
 // P.V product, rows without any kept block output 0.
 //
-// One CTA per (query block, head), 320 threads:
-//   warps 0-7   softmax / accumulate.  Warpgroup g (warps 4g..4g+3) owns key
-//               columns [64g, 64g+64) of S and value columns [64g, 64g+64) of
-//               O; thread (warp%4, lane) owns query row 32*(warp%4)+lane.  The
-//               two halves of a row exchange their partial max through shared
-//               memory each key block; partial row sums combine at the end.
-//   warp 8      TMA producer: Q once, then K and V tiles of each kept block
-//               into a 2-stage ring (128-byte swizzle, 64-column boxes).
-//   warp 9      MMA issuer: S_j = Q K_j^T (kind::f16, M=N=K=128) into one of
-//               two TMEM S buffers, O_j = P_j V_j into one of two TMEM O
-//               buffers; allocates / frees 512 TMEM columns.
-// Pipelining: S_{j+1} is issued before O_j so the tensor core computes the
-// next scores while the softmax warps work on block j.  O_j is accumulated
-// into registers (acc = acc * alpha_j + O_j), so no rescale of TMEM is ever
-// needed and every TMEM buffer has exactly one producer and one consumer.
+// Two kernels, both warp-specialised (TMA producer warp, one MMA-issuing thread,
+// softmax warpgroups) with S, P and O in tensor memory:
+//   bsa2  one query window per CTA, two CTAs per SM: short key lists (cross-
+//         attention's four context windows), where a co-resident CTA hides the
+//         per-CTA set-up.
+//   bsa6  two query windows per CTA sharing one score buffer (long lists: the
+//         self-attention over the streaming KV cache).
+// Both raise the running max lazily (only when a block's max exceeds it by more
+// than 2^8) and rescale O in tensor memory only then.
 #include <cstdlib>
 
 #include "common.cuh"
@@ -42,301 +36,6 @@ struct Args {
   __nv_bfloat16* out;
   int64_t ldo;  // H * 128
 };
-
-constexpr size_t kSmemBytes = (size_t)kTileBytes * (1 /*Q*/ + 2 /*K*/ + 2 /*V*/ + 1 /*P*/) +
-                              1024 /*align*/ + 4096 /*barriers + exchange*/;
-
-__global__ void __launch_bounds__(kThreads, 1)
-    bsa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const Args args) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~(uintptr_t)1023);
-  uint8_t* sQ = base;
-  uint8_t* sK = sQ + kTileBytes;        // 2 stages
-  uint8_t* sV = sK + 2 * kTileBytes;    // 2 stages
-  uint8_t* sP = sV + 2 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTileBytes);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [2]
-  uint64_t* s_empty = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_full = bars + 12;   // [2]
-  uint64_t* o_empty = bars + 14;  // [2]
-  uint64_t* x_bar = bars + 16;    // [2] max exchange
-  uint64_t* l_bar = bars + 18;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
-  float* xmax = reinterpret_cast<float*>(bars + 24);  // [2 parity][2 halves][128]
-  float* xl = xmax + 2 * 2 * 128;                     // [2 halves][128]
-
-  const int warp = warp_id_uniform();
-  const int lane = threadIdx.x & 31;
-  const int qb = blockIdx.x;
-  const int h = blockIdx.y;
-  const int64_t rowid = (int64_t)h * args.NQ + qb;
-  const int cnt = __ldg(args.cnt + rowid);
-  const int32_t* sel = args.sel + rowid * args.sel_stride;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 8);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 8);
-      mbar_init(&x_bar[i], kSoftmaxThreads);
-    }
-    mbar_init(p_full, 8);
-    mbar_init(l_bar, kSoftmaxThreads);
-    fence_mbar_init();
-  }
-  if (warp == 9) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S buffers at 0 / 128, O buffers at 256 / 384
-  const int col_q = h * kTile;
-
-  if (warp == 8) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0 && cnt > 0) {
-      prefetch_tmap(&tmQ);
-      prefetch_tmap(&tmK);
-      prefetch_tmap(&tmV);
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_2d(sQ, &tmQ, q_full, col_q, qb * kTile);
-      tma_load_2d(sQ + kAtom, &tmQ, q_full, col_q + 64, qb * kTile);
-      for (int j = 0; j < cnt; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, 0x201u)) break;
-        const int krow = __ldg(sel + j) * kTile;
-        mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-        tma_load_2d(sK + st * kTileBytes, &tmK, &k_full[st], col_q, krow);
-        tma_load_2d(sK + st * kTileBytes + kAtom, &tmK, &k_full[st], col_q + 64, krow);
-        mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-        tma_load_2d(sV + st * kTileBytes, &tmV, &v_full[st], col_q, krow);
-        tma_load_2d(sV + st * kTileBytes + kAtom, &tmV, &v_full[st], col_q + 64, krow);
-      }
-    }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && cnt > 0) {
-      constexpr uint32_t idesc_s = make_idesc(1 /*bf16*/, 1 /*bf16*/, 0, 0, 128, 128);
-      constexpr uint32_t idesc_o = make_idesc(1, 1, 0 /*P K-major*/, 1 /*V MN-major*/, 128, 128);
-      const uint32_t q0 = smem_u32(sQ);
-      const uint32_t p0 = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, 0x202u);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(&k_full[st], ph, 0x203u)) return false;
-        if (!mbar_wait(&s_empty[st], ph ^ 1u, 0x204u)) return false;
-        tc_fence_after();
-        const uint32_t k0 = smem_u32(sK + st * kTileBytes);
-        const uint32_t d = tmem + (uint32_t)(st * 128);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (uint32_t)((kk >> 2) * kAtom + (kk & 3) * 32);
-          mma_f16(d, smem_desc_sw128(q0 + off, 16, 1024), smem_desc_sw128(k0 + off, 16, 1024),
-                  idesc_s, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(&s_full[st]);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < cnt && ok; ++j) {
-        if (j + 1 < cnt && !issue_s(j + 1)) break;
-        const int st = j & 1;
-        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(p_full, (uint32_t)j & 1u, 0x205u)) break;
-        if (!mbar_wait(&v_full[st], ph, 0x206u)) break;
-        if (!mbar_wait(&o_empty[st], ph ^ 1u, 0x207u)) break;
-        tc_fence_after();
-        const uint32_t v0 = smem_u32(sV + st * kTileBytes);
-        const uint32_t d = tmem + 256u + (uint32_t)(st * 128);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t aoff = (uint32_t)((kk >> 2) * kAtom + (kk & 3) * 32);
-          mma_f16(d, smem_desc_sw128(p0 + aoff, 16, 1024),
-                  smem_desc_sw128(v0 + (uint32_t)(kk * 16 * 128), (uint32_t)kAtom, 1024), idesc_o,
-                  kk > 0 ? 1u : 0u);
-        }
-        tc_commit(&o_full[st]);
-        tc_commit(&kv_empty[st]);
-      }
-    }
-  } else {
-    // ------------------------------------------------------------ softmax warps
-    const int g = warp >> 2;        // column half
-    const int qr = warp & 3;        // TMEM lane quarter
-    const int row = qr * 32 + lane;  // query row within the block
-    const uint32_t lane_addr = (uint32_t)(qr * 32) << 16;
-    float acc[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-    bool ok = true;
-    uint8_t* prow = sP + g * kAtom + row * 128;
-    for (int j = 0; j < cnt; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-      if (!mbar_wait(&s_full[st], ph, 0x208u)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float s[64];
-      {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + (uint32_t)(st * 128 + g * 64), r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(r[i]);
-        tmem_ld_32x32b_x32(tmem + lane_addr + (uint32_t)(st * 128 + g * 64 + 32), r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 + i] = __uint_as_float(r[i]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[st]);
-      // scale into the log2 domain, mask keys past kv_len
-      const int key0 = __ldg(sel + j) * kTile + g * 64;
-      float pm = -INFINITY;
-      if (key0 + 64 <= args.kv_len) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          s[i] *= args.scale_log2;
-          pm = fmaxf(pm, s[i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          s[i] = (key0 + i < args.kv_len) ? s[i] * args.scale_log2 : -INFINITY;
-          pm = fmaxf(pm, s[i]);
-        }
-      }
-      // exchange the partial max with the other half of the row
-      float* xm = xmax + st * 256;
-      xm[g * 128 + row] = pm;
-      mbar_arrive(&x_bar[st]);
-      if (!mbar_wait(&x_bar[st], ph, 0x209u)) {
-        ok = false;
-        break;
-      }
-      const float m_new = fmaxf(m, fmaxf(pm, xm[(g ^ 1) * 128 + row]));
-      float alpha, msub;
-      if (m_new == -INFINITY) {  // nothing visible yet in this row
-        alpha = 1.f;
-        msub = 0.f;
-      } else {
-        alpha = exp2f(m - m_new);
-        msub = m_new;
-      }
-      uint32_t pk[32];
-      float ls = 0.f;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float p0 = exp2f(s[2 * i] - msub);
-        const float p1 = exp2f(s[2 * i + 1] - msub);
-        ls += p0 + p1;
-        __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-        pk[i] = *reinterpret_cast<uint32_t*>(&b2);
-      }
-      l = l * alpha + ls;
-      // fold in O_{j-1}; its completion also frees the P buffer
-      if (j > 0) {
-        const int ps = (j - 1) & 1;
-        const uint32_t pph = (uint32_t)((j - 1) >> 1) & 1u;
-        if (!mbar_wait(&o_full[ps], pph, 0x20Au)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + (uint32_t)(256 + ps * 128 + g * 64), r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = __fmaf_rn(acc[i], alpha_prev, __uint_as_float(r[i]));
-        tmem_ld_32x32b_x32(tmem + lane_addr + (uint32_t)(256 + ps * 128 + g * 64 + 32), r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          acc[32 + i] = __fmaf_rn(acc[32 + i], alpha_prev, __uint_as_float(r[i]));
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&o_empty[ps]);
-      }
-      alpha_prev = alpha;
-      // P_j (bf16, 64 keys of this half) into the swizzled K-major A operand
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = v;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      m = m_new;
-    }
-    if (ok && cnt > 0) {
-      const int ps = (cnt - 1) & 1;
-      const uint32_t pph = (uint32_t)((cnt - 1) >> 1) & 1u;
-      if (mbar_wait(&o_full[ps], pph, 0x20Bu)) {
-        tc_fence_after();
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + (uint32_t)(256 + ps * 128 + g * 64), r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = __fmaf_rn(acc[i], alpha_prev, __uint_as_float(r[i]));
-        tmem_ld_32x32b_x32(tmem + lane_addr + (uint32_t)(256 + ps * 128 + g * 64 + 32), r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          acc[32 + i] = __fmaf_rn(acc[32 + i], alpha_prev, __uint_as_float(r[i]));
-      } else {
-        ok = false;
-      }
-    }
-    // combine the two partial row sums
-    float lt = 0.f;
-    if (ok) {
-      xl[g * 128 + row] = l;
-      mbar_arrive(l_bar);
-      if (mbar_wait(l_bar, 0, 0x20Cu)) lt = l + xl[(g ^ 1) * 128 + row];
-    }
-    const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-    const int qrow = qb * kTile + row;
-    if (qrow < args.Lq) {
-      const int64_t orow = args.row_map ? (int64_t)__ldg(args.row_map + qrow) : (int64_t)qrow;
-      uint4* dst = reinterpret_cast<uint4*>(args.out + orow * args.ldo + col_q + g * 64);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float f[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = acc[8 * c + i] * inv;
-        dst[c] = f32_to_bf16x8(f);
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 9) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
 
 }  // namespace bsa
 
@@ -618,84 +317,93 @@ __global__ void __launch_bounds__(kThreads, 2)
 }  // namespace bsa2
 
 // ===========================================================================
-// v3: one CTA per SM, S double-buffered in TMEM, deep K/V prefetch.
+// bsa6: two query windows per CTA sharing ONE score buffer; P in its own TMEM columns.
 //
-// v2 runs S_j -> softmax_j -> P.V_j serially inside a CTA and single-buffers K and
-// V, so the TMA latency of the next key window sits on the critical path (ncu: tensor
-// pipe 40% active, issue slots 31%, stalls dominated by long-scoreboard waits).  v3
-// keeps one query tile per CTA but:
-//   * two S buffers in TMEM, so S_{j+1} = Q K_{j+1}^T runs while the softmax warps
-//     work on S_j; P_j overwrites (half of) S_j's buffer as packed bf16 and the
-//     P.V MMA reads it from TMEM; O accumulates in TMEM with the lazy rescale;
-//   * a 3-stage K ring and a 2-stage V ring (160 KB) + Q (32 KB), so TMA runs two
-//     windows ahead of the tensor core;
-//   * the MMA warp issues PV_j, then (once PV_j has released the buffer) S_{j+2}.
-// TMEM: S0 [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+// With P overlaid on S, the next S of a query window could only be issued after the
+// P.V reading P finished, and each window would run S -> softmax -> P.V strictly in
+// series.  Here each window ("item") has its own P columns and the two items take
+// turns in a single S buffer: as soon as an item's softmax warps have copied S into
+// registers (S_FREE), the MMA warp computes the other item's next S there.  The next S
+// of an item is therefore ready when its softmax finishes the current window, and the
+// softmax warpgroups run back to back.  What remains is the K/V stream: each key
+// window costs 64 KB of L2 -> shared memory traffic per 8.4 MFLOP, and the kernel runs
+// within ~20% of a copy of itself that only performs those loads.
+// TMEM: S [0,128), P_A [128,192), P_B [192,256), O_A [256,384), O_B [384,512).
+// MMA order: S_A0 S_B0 S_A1 | PV_A(j) S_B(j+1) PV_B(j) S_A(j+2) | ...; loads follow it.
 // ===========================================================================
-namespace bsa3 {
+namespace bsa6 {
 
-constexpr int kThreads = 320;
-constexpr int kSoftmaxThreads = 256;
+constexpr int kThreads = 320;  // warps 0-7 softmax (item = warp/4), 8 TMA, 9 MMA
 constexpr int kTile = 128;
 constexpr int kAtom = 128 * 128;
 constexpr int kTileBytes = 2 * kAtom;
-constexpr int kKStages = 3;
-constexpr int kVStages = 2;
 constexpr float kLazy = 8.0f;
+constexpr uint32_t kColS = 0, kColP = 128, kColO = 256;
 
-constexpr size_t kSmemBytes =
-    (size_t)kTileBytes * (1 + kKStages + kVStages) + 1024 /*align*/ + 3072 /*bars + xchg*/;
+constexpr size_t kSmemBytes = (size_t)kTileBytes * 6 + 1024 /*align*/ + 1024 /*bars*/;
+
+struct Item {
+  int qb;    // query window, -1 = none
+  int cnt;   // kept key windows
+  const int32_t* sel;
+};
+
+// p = 2^(s*c - m) for 64 scores -> 32 packed bf16 pairs; fp32 row sum into acc2.
+__device__ __forceinline__ void exp_pack64(const uint32_t* s, uint64_t cc, uint64_t nm,
+                                           uint64_t& acc2, uint32_t* pk) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const uint64_t xv = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), cc, nm);
+    float x0, x1;
+    f2_unpack(xv, x0, x1);
+    const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+    acc2 = f2_add(acc2, f2_pack(p0, p1));
+    __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+    pk[i] = *reinterpret_cast<uint32_t*>(&b2);
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
-    bsa_fwd_v3_kernel(const __grid_constant__ CUtensorMap tmQ,
+    bsa_fwd_v6_kernel(const __grid_constant__ CUtensorMap tmQ,
                       const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const bsa::Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
-  uint8_t* sQ = base;
-  uint8_t* sK = sQ + kTileBytes;               // kKStages tiles
-  uint8_t* sV = sK + kKStages * kTileBytes;    // kVStages tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVStages * kTileBytes);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;     // [3]
-  uint64_t* k_empty = bars + 4;    // [3]
-  uint64_t* v_full = bars + 7;     // [2]
-  uint64_t* v_empty = bars + 9;    // [2]
-  uint64_t* s_full = bars + 11;    // [2]
-  uint64_t* s_free = bars + 13;    // [2]  P of this buffer consumed by its P.V
-  uint64_t* p_full = bars + 15;    // [2]
-  uint64_t* pv_done = bars + 17;   // completes once per P.V, in order
-  uint64_t* x_bar = bars + 18;     // [2]
-  uint64_t* l_bar = bars + 20;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
-  float* xmax = reinterpret_cast<float*>(bars + 24);  // [2 parity][2 halves][128]
-  float* xl = xmax + 2 * 2 * 128;                     // [2 halves][128]
+  uint8_t* sQ[2] = {base, base + 3 * kTileBytes};
+  uint8_t* sK[2] = {base + kTileBytes, base + 4 * kTileBytes};
+  uint8_t* sV[2] = {base + 2 * kTileBytes, base + 5 * kTileBytes};
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 6 * kTileBytes);
+  enum { Q_FULL = 0, K_FULL, K_EMPTY, V_FULL, V_EMPTY, S_FULL, S_FREE, P_FULL, PV_DONE, kNB };
+  auto BAR = [&](int x, int i) { return bars + x * kNB + i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kNB);
 
   const int warp = warp_id_uniform();
   const int lane = threadIdx.x & 31;
-  const int qb = blockIdx.x;
   const int h = blockIdx.y;
-  const int64_t rowid = (int64_t)h * args.NQ + qb;
-  const int cnt = __ldg(args.cnt + rowid);
-  const int32_t* sel = args.sel + rowid * args.sel_stride;
+  Item it[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const int qb = blockIdx.x * 2 + x;
+    if (qb < args.NQ) {
+      const int64_t rowid = (int64_t)h * args.NQ + qb;
+      it[x].qb = qb;
+      it[x].cnt = __ldg(args.cnt + rowid);
+      it[x].sel = args.sel + rowid * args.sel_stride;
+    } else {
+      it[x].qb = -1;
+      it[x].cnt = 0;
+      it[x].sel = args.sel;
+    }
+  }
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < kKStages; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      // every barrier initialised exactly once; S_FREE and P_FULL collect one arrival
+      // per softmax warp of the item
+      for (int b = 0; b < kNB; ++b) mbar_init(BAR(x, b), (b == S_FREE || b == P_FULL) ? 4u : 1u);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 1);
-      mbar_init(&p_full[i], 8);
-      mbar_init(&x_bar[i], kSoftmaxThreads);
-    }
-    mbar_init(pv_done, 1);
-    mbar_init(l_bar, kSoftmaxThreads);
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -706,203 +414,227 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tO = tmem + 256;
   const int col_q = h * kTile;
+  const int jmax = it[0].cnt > it[1].cnt ? it[0].cnt : it[1].cnt;
 
   if (warp == 8) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0 && cnt > 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && jmax > 0) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_2d(sQ, &tmQ, q_full, col_q, qb * kTile);
-      tma_load_2d(sQ + kAtom, &tmQ, q_full, col_q + 64, qb * kTile);
-      for (int j = 0; j < cnt; ++j) {
-        const int krow = __ldg(sel + j) * kTile;
-        const int ks = j % kKStages;
-        if (!mbar_wait(&k_empty[ks], (uint32_t)((j / kKStages) & 1) ^ 1u, 0x401u)) break;
-        mbar_arrive_expect_tx(&k_full[ks], kTileBytes);
-        tma_load_2d(sK + ks * kTileBytes, &tmK, &k_full[ks], col_q, krow);
-        tma_load_2d(sK + ks * kTileBytes + kAtom, &tmK, &k_full[ks], col_q + 64, krow);
-        const int vs = j & 1;
-        if (!mbar_wait(&v_empty[vs], (uint32_t)((j >> 1) & 1) ^ 1u, 0x402u)) break;
-        mbar_arrive_expect_tx(&v_full[vs], kTileBytes);
-        tma_load_2d(sV + vs * kTileBytes, &tmV, &v_full[vs], col_q, krow);
-        tma_load_2d(sV + vs * kTileBytes + kAtom, &tmV, &v_full[vs], col_q + 64, krow);
+      bool ok = true;
+      auto load_k = [&](int x, int j) {
+        if (!ok || j >= it[x].cnt) return;
+        if (!mbar_wait(BAR(x, K_EMPTY), (uint32_t)(j & 1) ^ 1u, 0x701u)) { ok = false; return; }
+        const int krow = __ldg(it[x].sel + j) * kTile;
+        mbar_arrive_expect_tx(BAR(x, K_FULL), kTileBytes);
+        tma_load_2d(sK[x], &tmK, BAR(x, K_FULL), col_q, krow);
+        tma_load_2d(sK[x] + kAtom, &tmK, BAR(x, K_FULL), col_q + 64, krow);
+      };
+      auto load_v = [&](int x, int j) {
+        if (!ok || j >= it[x].cnt) return;
+        if (!mbar_wait(BAR(x, V_EMPTY), (uint32_t)(j & 1) ^ 1u, 0x702u)) { ok = false; return; }
+        const int krow = __ldg(it[x].sel + j) * kTile;
+        mbar_arrive_expect_tx(BAR(x, V_FULL), kTileBytes);
+        tma_load_2d(sV[x], &tmV, BAR(x, V_FULL), col_q, krow);
+        tma_load_2d(sV[x] + kAtom, &tmV, BAR(x, V_FULL), col_q + 64, krow);
+      };
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        if (it[x].cnt > 0) {
+          mbar_arrive_expect_tx(BAR(x, Q_FULL), kTileBytes);
+          tma_load_2d(sQ[x], &tmQ, BAR(x, Q_FULL), col_q, it[x].qb * kTile);
+          tma_load_2d(sQ[x] + kAtom, &tmQ, BAR(x, Q_FULL), col_q + 64, it[x].qb * kTile);
+        }
+      }
+      // same order as the MMA warp consumes them
+      load_k(0, 0);
+      load_k(1, 0);
+      for (int j = 0; j < jmax && ok; ++j) {
+        load_k(0, j + 1);
+        load_v(0, j);
+        load_k(1, j + 1);
+        load_v(1, j);
       }
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && cnt > 0) {
+    if (lane == 0 && jmax > 0) {
       constexpr uint32_t idesc_s = make_idesc(1 /*bf16*/, 1 /*bf16*/, 0, 0, 128, 128);
       constexpr uint32_t idesc_o = make_idesc(1, 1, 0 /*P K-major*/, 1 /*V MN-major*/, 128, 128);
-      const uint32_t q0 = smem_u32(sQ);
-      bool ok = mbar_wait(q_full, 0, 0x403u);
-      auto issue_s = [&](int j) -> bool {
-        const int ks = j % kKStages;
-        const int b = j & 1;
-        if (!mbar_wait(&k_full[ks], (uint32_t)((j / kKStages) & 1), 0x404u)) return false;
-        // buffer b last held P_{j-2}; its P.V must have consumed it
-        if (j >= 2 && !mbar_wait(&s_free[b], (uint32_t)(((j - 2) >> 1) & 1), 0x405u)) return false;
+      bool ok = true;
+      int last_x = -1, last_j = 0;  // owner of the S buffer's current contents
+      auto issue_s = [&](int x, int j) {
+        if (!ok || j >= it[x].cnt) return;
+        if (j == 0 && !mbar_wait(BAR(x, Q_FULL), 0, 0x703u)) { ok = false; return; }
+        // the previous S in the shared buffer must have been copied out by its softmax
+        if (last_x >= 0 && !mbar_wait(BAR(last_x, S_FREE), (uint32_t)(last_j & 1), 0x704u)) {
+          ok = false;
+          return;
+        }
+        if (!mbar_wait(BAR(x, K_FULL), (uint32_t)(j & 1), 0x705u)) { ok = false; return; }
         tc_fence_after();
-        const uint32_t k0 = smem_u32(sK + ks * kTileBytes);
-        const uint32_t d = tmem + (uint32_t)(b * 128);
+        const uint32_t q0 = smem_u32(sQ[x]);
+        const uint32_t k0 = smem_u32(sK[x]);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (uint32_t)((kk >> 2) * kAtom + (kk & 3) * 32);
-          mma_f16(d, smem_desc_sw128(q0 + off, 16, 1024), smem_desc_sw128(k0 + off, 16, 1024),
-                  idesc_s, kk > 0 ? 1u : 0u);
+          mma_f16(tmem + kColS, smem_desc_sw128(q0 + off, 16, 1024),
+                  smem_desc_sw128(k0 + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[b]);
-        tc_commit(&k_empty[ks]);
-        return true;
+        tc_commit(BAR(x, S_FULL));
+        tc_commit(BAR(x, K_EMPTY));
+        last_x = x;
+        last_j = j;
       };
-      if (ok) ok = issue_s(0);
-      if (ok && cnt > 1) ok = issue_s(1);
-      for (int j = 0; j < cnt && ok; ++j) {
-        const int b = j & 1;
-        if (!mbar_wait(&p_full[b], (uint32_t)((j >> 1) & 1), 0x406u)) break;
-        const int vs = j & 1;
-        if (!mbar_wait(&v_full[vs], (uint32_t)((j >> 1) & 1), 0x407u)) break;
+      auto issue_pv = [&](int x, int j) {
+        if (!ok || j >= it[x].cnt) return;
+        if (!mbar_wait(BAR(x, P_FULL), (uint32_t)(j & 1), 0x706u)) { ok = false; return; }
+        if (!mbar_wait(BAR(x, V_FULL), (uint32_t)(j & 1), 0x707u)) { ok = false; return; }
         tc_fence_after();
-        const uint32_t v0 = smem_u32(sV + vs * kTileBytes);
-        const uint32_t sb = tmem + (uint32_t)(b * 128);
+        const uint32_t v0 = smem_u32(sV[x]);
+        const uint32_t tP = tmem + kColP + (uint32_t)(x * 64);
+        const uint32_t tO = tmem + kColO + (uint32_t)(x * 128);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          // keys [16kk, 16kk+16): P of half g sits in columns [64g, 64g+32) of the buffer
-          const uint32_t pcol = (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
-          mma_f16_ts(tO, sb + pcol,
+          // keys [16kk, 16kk+16) are P columns [8kk, 8kk+8)
+          mma_f16_ts(tO, tP + (uint32_t)(kk * 8),
                      smem_desc_sw128(v0 + (uint32_t)(kk * 16 * 128), (uint32_t)kAtom, 1024),
                      idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        tc_commit(&v_empty[vs]);
-        tc_commit(&s_free[b]);
-        tc_commit(pv_done);
-        if (j + 2 < cnt) ok = issue_s(j + 2);
+        tc_commit(BAR(x, V_EMPTY));
+        tc_commit(BAR(x, PV_DONE));
+      };
+      issue_s(0, 0);
+      issue_s(1, 0);
+      issue_s(0, 1);
+      for (int j = 0; j < jmax && ok; ++j) {
+        issue_pv(0, j);
+        issue_s(1, j + 1);
+        issue_pv(1, j);
+        issue_s(0, j + 2);
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax warps
-    const int g = warp >> 2;         // key / value column half
+    // ------------------------------------------------------------ softmax warpgroups
+    const int x = warp >> 2;         // item of this warpgroup
     const int qr = warp & 3;         // TMEM lane quarter
-    const int row = qr * 32 + lane;  // query row within the block
+    const int row = qr * 32 + lane;  // query row within the window
     const uint32_t lane_addr = (uint32_t)(qr * 32) << 16;
+    const uint32_t tS = tmem + kColS + lane_addr;
+    const uint32_t tP = tmem + kColP + (uint32_t)(x * 64) + lane_addr;
+    const uint32_t tO = tmem + kColO + (uint32_t)(x * 128) + lane_addr;
+    const Item me = x ? it[1] : it[0];
     const float c = args.scale_log2;
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < cnt; ++j) {
-      const int b = j & 1;
-      const uint32_t tS = tmem + (uint32_t)(b * 128);
-      if (!mbar_wait(&s_full[b], (uint32_t)((j >> 1) & 1), 0x408u)) {
+    for (int j = 0; j < me.cnt; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(BAR(x, S_FULL), (uint32_t)(j & 1), 0x708u))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t s[64];
-      tmem_ld_32x32b_x32(tS + lane_addr + (uint32_t)(g * 64), s);
-      tmem_ld_32x32b_x32(tS + lane_addr + (uint32_t)(g * 64 + 32), s + 32);
+      uint32_t s[128];
+      tmem_ld_32x32b_x32(tS, s);
+      tmem_ld_32x32b_x32(tS + 32, s + 32);
+      tmem_ld_32x32b_x32(tS + 64, s + 64);
+      tmem_ld_32x32b_x32(tS + 96, s + 96);
       tmem_ld_wait();
-      const int key0 = __ldg(sel + j) * kTile + g * 64;
-      if (key0 + 64 > args.kv_len) {
+      // S is in registers: hand the buffer to the MMA warp for the other item's next S
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(x, S_FREE));
+      const int key0 = __ldg(me.sel + j) * kTile;
+      if (key0 + kTile > args.kv_len) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
+        for (int i = 0; i < 128; ++i)
           if (key0 + i >= args.kv_len) s[i] = __float_as_uint(-INFINITY);
       }
-      float pm = -INFINITY;
+      float mx[4];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) pm = fmaxf(pm, __uint_as_float(s[i]));
-      float* xm = xmax + (j & 1) * 256;
-      xm[g * 128 + row] = pm;
-      mbar_arrive(&x_bar[j & 1]);
-      if (!mbar_wait(&x_bar[j & 1], (uint32_t)(j >> 1) & 1u, 0x409u)) {
-        ok = false;
-        break;
+      for (int t = 0; t < 4; ++t)
+        mx[t] = fmax3(__uint_as_float(s[t]), __uint_as_float(s[4 + t]), __uint_as_float(s[8 + t]));
+#pragma unroll
+      for (int i = 12; i < 124; i += 8) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          mx[t] = fmax3(mx[t], __uint_as_float(s[i + t]), __uint_as_float(s[i + 4 + t]));
       }
-      const float mb = fmaxf(pm, xm[(g ^ 1) * 128 + row]) * c;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) mx[t] = fmaxf(mx[t], __uint_as_float(s[124 + t]));
+      const float mb = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c;  // log2 domain
       float alpha = 1.f;
-      const bool raise = mb > m_used + kLazy;
-      if (raise) {
+      const bool rescale = mb > m_used + kLazy;
+      if (rescale) {
         alpha = (m_used == -INFINITY) ? 0.f : ex2_approx(m_used - mb);
         m_used = mb;
       }
       const float msub = (m_used == -INFINITY) ? 0.f : m_used;
       const uint64_t cc = f2_pack(c, c);
       const uint64_t nm = f2_pack(-msub, -msub);
-      uint32_t pk[32];
       uint64_t acc2 = f2_pack(0.f, 0.f);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const uint64_t x = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])),
-                                  cc, nm);
-        float x0, x1;
-        f2_unpack(x, x0, x1);
-        const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
-        acc2 = f2_add(acc2, f2_pack(p0, p1));
-        __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-        pk[i] = *reinterpret_cast<uint32_t*>(&b2);
-      }
-      float la, lb;
-      f2_unpack(acc2, la, lb);
-      l = l * alpha + (la + lb);
-      tmem_st_32x32b_x32(tS + lane_addr + (uint32_t)(g * 64), pk);
-      if (raise && j > 0) {
-        // O holds P.V of windows < j; the P.V of window j-1 may still be running
-        if (!mbar_wait(pv_done, (uint32_t)((j - 1) & 1), 0x40Au)) {
+      uint32_t pk[32];
+      exp_pack64(s, cc, nm, acc2, pk);
+      if (j > 0) {
+        // P_X and O_X are free once the P.V of window j-1 completed
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait(BAR(x, PV_DONE), (uint32_t)((j - 1) & 1), 0x709u))) {
           ok = false;
           break;
         }
         tc_fence_after();
+        if (rescale) {
+#pragma unroll 1
+          for (int hh = 0; hh < 4; ++hh) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(tO + (uint32_t)(hh * 32), o);
+            tmem_ld_wait();
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t o[32];
-          const uint32_t oa = tO + lane_addr + (uint32_t)(g * 64 + hh * 32);
-          tmem_ld_32x32b_x32(oa, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st_32x32b_x32(oa, o);
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_32x32b_x32(tO + (uint32_t)(hh * 32), o);
+          }
         }
       }
+      tmem_st_32x32b_x32(tP, pk);  // keys [0,64) -> P columns [0,32)
+      exp_pack64(s + 64, cc, nm, acc2, pk);
+      tmem_st_32x32b_x32(tP + 32, pk);  // keys [64,128) -> P columns [32,64)
+      float la, lb;
+      f2_unpack(acc2, la, lb);
+      l = l * alpha + (la + lb);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (lane == 0) mbar_arrive(BAR(x, P_FULL));
     }
-    float lt = 0.f;
-    bool have_o = false;
-    if (ok && cnt > 0 && mbar_wait(pv_done, (uint32_t)((cnt - 1) & 1), 0x40Bu)) {
-      tc_fence_after();
-      xl[g * 128 + row] = l;
-      mbar_arrive(l_bar);
-      if (mbar_wait(l_bar, 0, 0x40Cu)) {
-        lt = l + xl[(g ^ 1) * 128 + row];
-        have_o = true;
-      }
-    }
-    const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-    const int qrow = qb * kTile + row;
-    const int64_t orow =
-        args.row_map ? (int64_t)__ldg(args.row_map + (qrow < args.Lq ? qrow : 0)) : (int64_t)qrow;
-    uint4* dst = reinterpret_cast<uint4*>(args.out + orow * args.ldo + col_q + g * 64);
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      uint32_t o[32];
-      if (have_o) {
-        tmem_ld_32x32b_x32(tO + lane_addr + (uint32_t)(g * 64 + hh * 32), o);
-        tmem_ld_wait();
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0u;
-      }
+    const bool have_o = __all_sync(
+        0xffffffffu,
+        ok && me.cnt > 0 && mbar_wait(BAR(x, PV_DONE), (uint32_t)((me.cnt - 1) & 1), 0x70au));
+    if (have_o) tc_fence_after();
+    const float inv = (have_o && l > 0.f) ? 1.0f / l : 0.f;
+    if (me.qb >= 0) {
+      const int qrow = me.qb * kTile + row;
       if (qrow < args.Lq) {
+        const int64_t orow = args.row_map ? (int64_t)__ldg(args.row_map + qrow) : (int64_t)qrow;
+        uint4* dst = reinterpret_cast<uint4*>(args.out + orow * args.ldo + col_q);
+#pragma unroll 1
+        for (int hh = 0; hh < 4; ++hh) {
+          uint32_t o[32];
+          if (have_o) {
+            tmem_ld_32x32b_x32(tO + (uint32_t)(hh * 32), o);
+            tmem_ld_wait();
+          } else {
 #pragma unroll
-        for (int cch = 0; cch < 4; ++cch) {
-          float f[8];
+            for (int i = 0; i < 32; ++i) o[i] = 0u;
+          }
 #pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(o[8 * cch + i]) * inv;
-          dst[hh * 4 + cch] = f32_to_bf16x8(f);
+          for (int cch = 0; cch < 4; ++cch) {
+            float f[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(o[8 * cch + i]) * inv;
+            dst[hh * 4 + cch] = f32_to_bf16x8(f);
+          }
         }
       }
     }
@@ -915,7 +647,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-}  // namespace bsa3
+}  // namespace bsa6
+
 }  // namespace fvb
 
 extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const int32_t* sel,
@@ -945,31 +678,27 @@ extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const in
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   static bool configured[64] = {false};
-  // Kernel generation: v3 (1 CTA/SM, deep prefetch) when the key list can be long, v2
-  // (2 CTAs/SM) for short lists such as cross-attention's 4 windows, where a co-resident
-  // CTA hides the per-CTA set-up.  FVB_BSA_IMPL=v1|v2|v3 pins one (A/B timing).
+  // bsa6 (two query windows per CTA) when the key list can be long, bsa2 (two CTAs per
+  // SM) for short lists such as cross-attention's four windows, where a co-resident CTA
+  // hides the per-CTA set-up.  FVB_BSA_IMPL=v2|v6 pins one (A/B timing).
   static int forced = -1;
   if (forced < 0) {
     const char* e = getenv("FVB_BSA_IMPL");
-    forced = (e && e[0] == 'v' && e[1] >= '1' && e[1] <= '3') ? (e[1] - '0') : 0;
+    forced = (e && e[0] == 'v' && (e[1] == '2' || e[1] == '6')) ? (e[1] - '0') : 0;
   }
   const int64_t nk_blocks = Lk / 128;
-  const int impl = forced ? forced : (nk_blocks >= 16 ? 3 : 2);
+  const int impl = forced ? forced : (nk_blocks >= 16 ? 6 : 2);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    FVB_CUDA_TRY(cudaFuncSetAttribute(bsa::bsa_fwd_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)bsa::kSmemBytes),
-                 "bsa smem attribute");
     FVB_CUDA_TRY(cudaFuncSetAttribute(bsa2::bsa_fwd_v2_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)bsa2::kSmemBytes),
                  "bsa2 smem attribute");
-    FVB_CUDA_TRY(cudaFuncSetAttribute(bsa3::bsa_fwd_v3_kernel,
+    FVB_CUDA_TRY(cudaFuncSetAttribute(bsa6::bsa_fwd_v6_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)bsa3::kSmemBytes),
-                 "bsa3 smem attribute");
+                                      (int)bsa6::kSmemBytes),
+                 "bsa6 smem attribute");
     configured[dev] = true;
   }
   bsa::Args a;
@@ -984,14 +713,11 @@ extern "C" int fvb_bsa_fwd(const void* q, const void* k, const void* v, const in
   a.row_map = out_row_map;
   a.out = (__nv_bfloat16*)out;
   a.ldo = (int64_t)HD;
-  if (impl == 1)
-    bsa::bsa_fwd_kernel<<<dim3((unsigned)NQ, (unsigned)H), bsa::kThreads, bsa::kSmemBytes,
-                          (cudaStream_t)stream>>>(tq, tk, tv, a);
-  else if (impl == 2)
+  if (impl == 2)
     bsa2::bsa_fwd_v2_kernel<<<dim3((unsigned)NQ, (unsigned)H), bsa2::kThreads,
                               bsa2::kSmemBytes, (cudaStream_t)stream>>>(tq, tk, tv, a);
   else
-    bsa3::bsa_fwd_v3_kernel<<<dim3((unsigned)NQ, (unsigned)H), bsa3::kThreads,
-                              bsa3::kSmemBytes, (cudaStream_t)stream>>>(tq, tk, tv, a);
+    bsa6::bsa_fwd_v6_kernel<<<dim3((unsigned)((NQ + 1) / 2), (unsigned)H), bsa6::kThreads,
+                              bsa6::kSmemBytes, (cudaStream_t)stream>>>(tq, tk, tv, a);
   return check_launch("fvb_bsa_fwd");
 }

@@ -350,6 +350,12 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ float fmax3(float a, float b, float c) {  // sm_100 3-input max
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 
 // Shared-memory matrix descriptor for a tcgen05 operand tile in the 128-byte
 // swizzled canonical layout (8-row x 128-byte atoms, 1024-byte aligned base).

@@ -277,6 +277,32 @@ def sparse_attention(q_w, k_w, v_w, keep):
     return out.permute(1, 2, 0, 3).reshape(NQ, S, C)
 
 
+def _online_pass(qi, kh, vh, blocks, c, kv_len, lazy, S, d):
+    """Online softmax over the key blocks `blocks` in the given order; returns (m, l, acc)
+    with m the max the exponentials were taken against (log2 units, -inf if none)."""
+    m = torch.full((S,), float("-inf"))
+    l = torch.zeros(S)
+    acc = torch.zeros(S, d)
+    for j in blocks:
+        s = (qi @ kh[j].t()) * c
+        if kv_len is not None and (j + 1) * S > kv_len:
+            cols = torch.arange(j * S, (j + 1) * S)
+            s[:, cols >= kv_len] = float("-inf")
+        mb = s.max(dim=1).values
+        if lazy > 0:
+            m_new = torch.where(mb > m + lazy, mb, m)
+        else:
+            m_new = torch.maximum(m, mb)
+        safe = torch.where(torch.isinf(m_new), torch.zeros_like(m_new), m_new)
+        alpha = torch.where(torch.isinf(m_new), torch.ones_like(m),
+                            torch.where(torch.isinf(m), torch.zeros_like(m), torch.exp2(m - safe)))
+        p = torch.exp2(s - safe[:, None])
+        l = l * alpha + p.sum(dim=1)
+        acc = acc * alpha[:, None] + p.to(torch.bfloat16).float() @ vh[j]
+        m = m_new
+    return m, l, acc
+
+
 def sparse_attention_online(q_w, k_w, v_w, keep, kv_len=None, lazy=0.0):
     """The reference kernel's evaluation order (lcsa/triton_lcsa.py:44-59): per (head, query
     block), kept key blocks in ascending order, online softmax in the log2 domain with fp32
@@ -296,26 +322,8 @@ def sparse_attention_online(q_w, k_w, v_w, keep, kv_len=None, lazy=0.0):
     out = torch.zeros_like(q)
     for h in range(H):
         for i in range(NQ):
-            m = torch.full((S,), float("-inf"))
-            l = torch.zeros(S)
-            acc = torch.zeros(S, d)
-            for j in keep[h, i].nonzero(as_tuple=True)[0].tolist():
-                s = (q[h, i] @ k[h, j].t()) * c
-                if kv_len is not None and (j + 1) * S > kv_len:
-                    cols = torch.arange(j * S, (j + 1) * S)
-                    s[:, cols >= kv_len] = float("-inf")
-                mb = s.max(dim=1).values
-                if lazy > 0:
-                    m_new = torch.where(mb > m + lazy, mb, m)
-                else:
-                    m_new = torch.maximum(m, mb)
-                safe = torch.where(torch.isinf(m_new), torch.zeros_like(m_new), m_new)
-                alpha = torch.where(torch.isinf(m_new), torch.ones_like(m),
-                                    torch.where(torch.isinf(m), torch.zeros_like(m), torch.exp2(m - safe)))
-                p = torch.exp2(s - safe[:, None])
-                l = l * alpha + p.sum(dim=1)
-                acc = acc * alpha[:, None] + p.to(torch.bfloat16).float() @ v[h, j]
-                m = m_new
+            blocks = keep[h, i].nonzero(as_tuple=True)[0].tolist()
+            m, l, acc = _online_pass(q[h, i], k[h], v[h], blocks, c, kv_len, lazy, S, d)
             out[h, i] = torch.where(l[:, None] > 0, acc / l.clamp(min=1e-30)[:, None],
                                     torch.zeros_like(acc))
     return out.permute(1, 2, 0, 3).reshape(NQ, S, C)

@@ -277,6 +277,39 @@ def test_block_sparse_attention(h_lat, w_lat, nk_extra, ratio):
     assert out[0, :S, :Dh].abs().max().item() == 0.0
 
 
+def test_long_list_attention_kernel_order():
+    """Key lists of >= 16 blocks take the two-window kernel (two query windows per CTA sharing
+    one score buffer).  An odd number of query windows (the last CTA has one), rows with 0, 1,
+    2, 3 kept blocks, a ragged key tail (kv_len) and a row map; checked against the oracle's
+    restatement of the kernel's evaluation order (tight) and the reference order (loose)."""
+    from flashvsr_sm89_ops_b200.lcsa import attention_csr, build_csr
+    H, Dh, S, NQ, NK = 4, 128, 128, 7, 20
+    g = gen(17)
+    q_w = torch.randn(NQ, S, H * Dh, generator=g).to(torch.bfloat16)
+    k_w = torch.randn(NK, S, H * Dh, generator=g).to(torch.bfloat16)
+    v_w = torch.randn(NK, S, H * Dh, generator=g).to(torch.bfloat16)
+    keep = torch.rand(H, NQ, NK, generator=g) < 0.5
+    for i, n in enumerate([0, 1, 2, 3]):
+        keep[i % H, i] = False
+        keep[i % H, i, torch.randperm(NK, generator=g)[:n]] = True
+    keep[:, 5, NK - 1] = True  # the tail block (partly past kv_len)
+    kv_len = NK * S - 37
+    sel, cnt, _ = build_csr(keep.to(DEV))
+    row_map = torch.randperm(NQ * S, generator=g).to(torch.int32)
+    out = attention_csr(q_w.reshape(-1, H * Dh).to(DEV), k_w.reshape(-1, H * Dh).to(DEV),
+                        v_w.reshape(-1, H * Dh).to(DEV), sel, cnt, H, kv_len=kv_len,
+                        row_map=row_map.to(DEV))
+    got = torch.empty_like(out)
+    got[torch.arange(NQ * S, device=DEV)] = out[row_map.long().to(DEV)]
+    got = got.float().cpu().view(NQ, S, H * Dh)
+    ref = O.sparse_attention_online(q_w, k_w, v_w, keep, kv_len=kv_len, lazy=8.0)
+    assert (got - ref).abs().max().item() < 2e-2
+    assert (got - ref).norm().item() / ref.norm().item() < 3e-3
+    ref32 = O.sparse_attention_online(q_w, k_w, v_w, keep, kv_len=kv_len)  # reference order
+    assert torch.allclose(got, ref32, atol=1e-2, rtol=1e-2)
+    assert got[0].view(S, H, Dh)[:, 0].abs().max().item() == 0.0  # row with no kept block
+
+
 def test_dense_attention_cross():
     from flashvsr_sm89_ops_b200.lcsa import dense_attention
     H, Dh = 12, 128
