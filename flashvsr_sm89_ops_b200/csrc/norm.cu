@@ -14,17 +14,77 @@
 //   fused_adaln.py:53-57  out = bf16(x + bf16(g * r))
 //   fused_rms_rope.py:34-53  y = bf16(x * rsqrt(mean(x^2)+eps)) * w (fp32),
 //                          even: y_e c - y_o s, odd: y_o c + y_e s, one bf16 rounding
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace fvb {
-
-constexpr int kRowNV = 8;  // vectors per lane -> D <= 8 * 8 * 32 = 2048
 
 __device__ __forceinline__ float quant_scale_from_amax_n(float amax) {
   return __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
 }
 
-template <bool EMIT_FP8>
+// Per-token e4m3 codes of 8 bf16 values held in a uint4 (the bf16 output of a row kernel):
+// q = e4m3_rn_satfinite(clamp(y / qs)), with the divide of div_for_e4m3.
+__device__ __forceinline__ uint2 fp8_codes8(const uint4& y, float qs, float rqs) {
+  float f[8];
+  bf16x8_to_f32(y, f);
+  uint32_t w[2];
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    float a[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) a[t] = fminf(fmaxf(div_for_e4m3(f[4 * hh + t], qs, rqs), -448.f), 448.f);
+    w[hh] = (uint32_t)f32x2_to_e4m3x2(a[0], a[1]) | ((uint32_t)f32x2_to_e4m3x2(a[2], a[3]) << 16);
+  }
+  return make_uint2(w[0], w[1]);
+}
+
+// Row mean and (x - mean) * rden with rden = 1/sqrt(var + eps), two-pass in registers.
+// x holds NV 16-byte vectors per lane (bf16); sums use packed fp32 pairs.
+template <int NV>
+__device__ __forceinline__ void row_stats(const uint4* xr, int lane, int nvec, int D, float eps,
+                                          float& mean, float& rden) {
+  uint64_t s2 = f2_pack(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    if (j * 32 + lane < nvec) {
+      float f[8];
+      bf16x8_to_f32(xr[j], f);
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) s2 = f2_add(s2, f2_pack(f[i], f[i + 1]));
+    }
+  }
+  float sa, sb;
+  f2_unpack(s2, sa, sb);
+  mean = __fdiv_rn(warp_sum(sa + sb), (float)D);
+  const uint64_t nm = f2_pack(-mean, -mean);
+  uint64_t q2 = f2_pack(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    if (j * 32 + lane < nvec) {
+      float f[8];
+      bf16x8_to_f32(xr[j], f);
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const uint64_t d = f2_add(f2_pack(f[i], f[i + 1]), nm);
+        q2 = f2_fma(d, d, q2);
+      }
+    }
+  }
+  float qa, qb;
+  f2_unpack(q2, qa, qb);
+  // (x - mean) / sqrt(var + eps) as a product with the correctly rounded reciprocal square
+  // root: at most one fp32 ulp from the quotient, well inside the bf16 rounding that follows
+  rden = __frsqrt_rn(__fdiv_rn(warp_sum(qa + qb), (float)D) + eps);
+}
+
+// LayerNorm + AdaLN modulate.  The modulate chain is bf16 arithmetic on bf16 operands:
+// xn * bf16(1 + scale) and (.) + shift are exact fp32 operations followed by one bf16
+// rounding in the reference; the packed bf16x2 instructions (non-contracting _rn forms) round
+// the exact result once, which is the same value (fp32 carries more than twice bf16's
+// precision plus two bits, so the fp32 intermediate never changes a bf16 rounding).
+template <bool EMIT_FP8, int NV>
 __global__ void __launch_bounds__(256) ln_modulate_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ scale,
     const __nv_bfloat16* __restrict__ shift, int64_t rows, int64_t L, int D, float eps,
@@ -33,56 +93,113 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int nvec = D >> 3;
-  const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
-  float f[kRowNV][8];
-  float sum = 0.f;
-#pragma unroll
-  for (int j = 0; j < kRowNV; ++j) {
-    int v = j * 32 + lane;
-    if (v < nvec) {
-      bf16x8_to_f32(__ldg(xv + v), f[j]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sum += f[j][i];
-    }
-  }
-  const float mean = __fdiv_rn(warp_sum(sum), (float)D);
-  float sq = 0.f;
-#pragma unroll
-  for (int j = 0; j < kRowNV; ++j) {
-    int v = j * 32 + lane;
-    if (v < nvec) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float d = f[j][i] - mean;
-        sq = __fmaf_rn(d, d, sq);
-      }
-    }
-  }
-  const float var = __fdiv_rn(warp_sum(sq), (float)D);
-  // (x - mean) / sqrt(var + eps) as a product with the correctly rounded reciprocal square
-  // root: at most one fp32 ulp from the quotient, well inside the bf16 rounding that follows
-  const float rden = __frsqrt_rn(var + eps);
   const int64_t b = row / L;
+  const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
   const uint4* sv = reinterpret_cast<const uint4*>(scale + b * D);
   const uint4* hv = reinterpret_cast<const uint4*>(shift + b * D);
-  uint4* ov = reinterpret_cast<uint4*>(out + row * D);
-  float amax = 0.f;
+  uint4 xr[NV], sr[NV], hr[NV];
 #pragma unroll
-  for (int j = 0; j < kRowNV; ++j) {
-    int v = j * 32 + lane;
+  for (int j = 0; j < NV; ++j) {
+    const int v = j * 32 + lane;
     if (v < nvec) {
-      float s[8], h[8];
-      bf16x8_to_f32(__ldg(sv + v), s);
-      bf16x8_to_f32(__ldg(hv + v), h);
+      xr[j] = __ldg(xv + v);
+      sr[j] = __ldg(sv + v);
+      hr[j] = __ldg(hv + v);
+    }
+  }
+  float mean, rden;
+  row_stats<NV>(xr, lane, nvec, D, eps, mean, rden);
+  const uint64_t nm = f2_pack(-mean, -mean), rd = f2_pack(rden, rden);
+  const __nv_bfloat162 one2 = __float2bfloat162_rn(1.0f);
+  __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
+  uint4* ov = reinterpret_cast<uint4*>(out + row * D);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int v = j * 32 + lane;
+    if (v < nvec) {
+      float f[8];
+      bf16x8_to_f32(xr[j], f);
+      const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&sr[j]);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&hr[j]);
+      uint4 yo;
+      __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&yo);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        float a, c;
+        f2_unpack(f2_mul(f2_add(f2_pack(f[2 * p], f[2 * p + 1]), nm), rd), a, c);
+        const __nv_bfloat162 xn = __floats2bfloat162_rn(a, c);
+        // _rn forms: no contraction of the multiply and the add into one bf16 fma
+        const __nv_bfloat162 y = __hadd2_rn(__hmul2_rn(xn, __hadd2_rn(one2, s2[p])), h2[p]);
+        y2[p] = y;
+        if (EMIT_FP8) m2 = __hmax2(m2, __habs2(y));
+      }
+      ov[v] = yo;
+      xr[j] = yo;
+    }
+  }
+  if (EMIT_FP8) {
+    const float2 mf = __bfloat1622float2(m2);
+    const float amax = warp_max(fmaxf(mf.x, mf.y));
+    const float qs = quant_scale_from_amax_n(amax);
+    const float rqs = __frcp_rn(qs);
+    uint2* qv = reinterpret_cast<uint2*>(q8 + row * D);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = j * 32 + lane;
+      if (v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
+    }
+    if (lane == 0) q_scale[row] = __fdiv_rn(amax, 448.0f);
+  }
+}
+
+// LayerNorm with optional affine weight / bias, fp32 math and one bf16 rounding (the
+// semantics of torch.nn.LayerNorm on bf16 tensors); optionally also the per-token e4m3
+// codes of that bf16 output (what the next FP8 linear would compute from it).
+template <bool EMIT_FP8, int NV>
+__global__ void __launch_bounds__(256) layer_norm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const __nv_bfloat16* __restrict__ w,
+                                                          const __nv_bfloat16* __restrict__ bias,
+                                                          int64_t rows, int D, float eps,
+                                                          __nv_bfloat16* __restrict__ out,
+                                                          uint8_t* __restrict__ q8,
+                                                          float* __restrict__ q_scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nvec = D >> 3;
+  const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
+  uint4 xr[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+    if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+  float mean, rstd;
+  row_stats<NV>(xr, lane, nvec, D, eps, mean, rstd);
+  float amax = 0.f;
+  uint4* ov = reinterpret_cast<uint4*>(out + row * D);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int v = j * 32 + lane;
+    if (v < nvec) {
+      float f[8], ww[8], bb[8];
+      bf16x8_to_f32(xr[j], f);
+      if (w) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), ww);
+      if (bias) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(bias) + v), bb);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        float xn = bf16r((f[j][i] - mean) * rden);
-        float y = bf16r(xn * bf16r(1.0f + s[i]));
-        y = bf16r(y + h[i]);
-        f[j][i] = y;
-        amax = fmaxf(amax, fabsf(y));
+        float y = (f[i] - mean) * rstd;
+        if (w) y = y * ww[i];
+        if (bias) y = y + bb[i];
+        f[i] = y;
       }
-      ov[v] = f32_to_bf16x8(f[j]);
+      const uint4 yo = f32_to_bf16x8(f);
+      ov[v] = yo;
+      if (EMIT_FP8) {
+        float r[8];
+        bf16x8_to_f32(yo, r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(r[i]));
+        xr[j] = yo;
+      }
     }
   }
   if (EMIT_FP8) {
@@ -91,79 +208,11 @@ __global__ void __launch_bounds__(256) ln_modulate_kernel(
     const float rqs = __frcp_rn(qs);
     uint2* qv = reinterpret_cast<uint2*>(q8 + row * D);
 #pragma unroll
-    for (int j = 0; j < kRowNV; ++j) {
-      int v = j * 32 + lane;
-      if (v < nvec) {
-        uint32_t w[2];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float a0 = fminf(fmaxf(div_for_e4m3(f[j][4 * hh + 0], qs, rqs), -448.f), 448.f);
-          float a1 = fminf(fmaxf(div_for_e4m3(f[j][4 * hh + 1], qs, rqs), -448.f), 448.f);
-          float a2 = fminf(fmaxf(div_for_e4m3(f[j][4 * hh + 2], qs, rqs), -448.f), 448.f);
-          float a3 = fminf(fmaxf(div_for_e4m3(f[j][4 * hh + 3], qs, rqs), -448.f), 448.f);
-          w[hh] = (uint32_t)f32x2_to_e4m3x2(a0, a1) | ((uint32_t)f32x2_to_e4m3x2(a2, a3) << 16);
-        }
-        qv[v] = make_uint2(w[0], w[1]);
-      }
+    for (int j = 0; j < NV; ++j) {
+      const int v = j * 32 + lane;
+      if (v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
     }
     if (lane == 0) q_scale[row] = __fdiv_rn(amax, 448.0f);
-  }
-}
-
-// LayerNorm with optional affine weight / bias, fp32 math and one bf16 rounding
-// (the semantics of torch.nn.LayerNorm on bf16 tensors).
-__global__ void __launch_bounds__(256) layer_norm_kernel(const __nv_bfloat16* __restrict__ x,
-                                                          const __nv_bfloat16* __restrict__ w,
-                                                          const __nv_bfloat16* __restrict__ bias,
-                                                          int64_t rows, int D, float eps,
-                                                          __nv_bfloat16* __restrict__ out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int nvec = D >> 3;
-  const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
-  float f[kRowNV][8];
-  float sum = 0.f;
-#pragma unroll
-  for (int j = 0; j < kRowNV; ++j) {
-    int v = j * 32 + lane;
-    if (v < nvec) {
-      bf16x8_to_f32(__ldg(xv + v), f[j]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sum += f[j][i];
-    }
-  }
-  const float mean = __fdiv_rn(warp_sum(sum), (float)D);
-  float sq = 0.f;
-#pragma unroll
-  for (int j = 0; j < kRowNV; ++j) {
-    int v = j * 32 + lane;
-    if (v < nvec) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float d = f[j][i] - mean;
-        sq = __fmaf_rn(d, d, sq);
-      }
-    }
-  }
-  const float rstd = __frsqrt_rn(__fdiv_rn(warp_sum(sq), (float)D) + eps);
-  uint4* ov = reinterpret_cast<uint4*>(out + row * D);
-#pragma unroll
-  for (int j = 0; j < kRowNV; ++j) {
-    int v = j * 32 + lane;
-    if (v < nvec) {
-      float ww[8], bb[8];
-      if (w) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), ww);
-      if (bias) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(bias) + v), bb);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float y = (f[j][i] - mean) * rstd;
-        if (w) y = y * ww[i];
-        if (bias) y = y + bb[i];
-        f[j][i] = y;
-      }
-      ov[v] = f32_to_bf16x8(f[j]);
-    }
   }
 }
 
@@ -191,7 +240,10 @@ __global__ void __launch_bounds__(256) gate_add_kernel(const uint4* __restrict__
   }
 }
 
-template <bool ROPE>
+// RMSNorm (+ interleaved RoPE).  y = bf16(x * rrms) * w in fp32 (an exact product of two
+// bf16 values); the rotation rounds each product and the sum once, all in packed fp32 pairs
+// (mul.rn / add.rn per lane, no contraction), then one bf16 rounding.
+template <bool ROPE, int NV>
 __global__ void __launch_bounds__(256) rms_rope_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t x_ld, const __nv_bfloat16* __restrict__ w,
     const float* __restrict__ cosv, const float* __restrict__ sinv, int64_t rows, int64_t L,
@@ -202,53 +254,81 @@ __global__ void __launch_bounds__(256) rms_rope_kernel(
   if (row >= rows) return;
   const int nvec = D >> 3;
   const uint4* xv = reinterpret_cast<const uint4*>(x + row * x_ld);
-  float f[kRowNV][8];
-  float sq = 0.f;
+  uint4 xr[NV];
 #pragma unroll
-  for (int j = 0; j < kRowNV; ++j) {
-    int v = j * 32 + lane;
-    if (v < nvec) {
-      bf16x8_to_f32(__ldg(xv + v), f[j]);
+  for (int j = 0; j < NV; ++j)
+    if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+  uint64_t q2 = f2_pack(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sq = __fmaf_rn(f[j][i], f[j][i], sq);
+  for (int j = 0; j < NV; ++j) {
+    if (j * 32 + lane < nvec) {
+      float f[8];
+      bf16x8_to_f32(xr[j], f);
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const uint64_t t = f2_pack(f[i], f[i + 1]);
+        q2 = f2_fma(t, t, q2);
+      }
     }
   }
-  const float rrms = __frsqrt_rn(__fdiv_rn(warp_sum(sq), (float)D) + eps);
-  const int64_t s = row % L;
+  float qa, qb;
+  f2_unpack(q2, qa, qb);
+  const float rrms = __frsqrt_rn(__fdiv_rn(warp_sum(qa + qb), (float)D) + eps);
+  const uint64_t rr = f2_pack(rrms, rrms);
+  const int64_t srow = row % L;
   const int half = head_dim >> 1;
   const int64_t orow = row_map ? (int64_t)__ldg(row_map + row) : row;
   uint4* ov = reinterpret_cast<uint4*>(out + orow * D);
 #pragma unroll
-  for (int j = 0; j < kRowNV; ++j) {
-    int v = j * 32 + lane;
+  for (int j = 0; j < NV; ++j) {
+    const int v = j * 32 + lane;
     if (v < nvec) {
-      float wf[8];
+      float f[8], wf[8];
+      bf16x8_to_f32(xr[j], f);
       bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), wf);
-      float y[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = bf16r(f[j][i] * rrms) * wf[i];
+      float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f), s4 = c4;
       if (ROPE) {
         const int pair0 = ((v * 8) % head_dim) >> 1;  // 4 consecutive pairs
-        const float4 c = __ldg(reinterpret_cast<const float4*>(cosv + s * half + pair0));
-        const float4 sn = __ldg(reinterpret_cast<const float4*>(sinv + s * half + pair0));
-        const float cc[4] = {c.x, c.y, c.z, c.w};
-        const float ss[4] = {sn.x, sn.y, sn.z, sn.w};
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const float ye = y[2 * p], yo = y[2 * p + 1];
-          f[j][2 * p] = __fadd_rn(__fmul_rn(ye, cc[p]), __fmul_rn(yo, -ss[p]));
-          f[j][2 * p + 1] = __fadd_rn(__fmul_rn(yo, cc[p]), __fmul_rn(ye, ss[p]));
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) f[j][i] = y[i];
+        c4 = __ldg(reinterpret_cast<const float4*>(cosv + srow * half + pair0));
+        s4 = __ldg(reinterpret_cast<const float4*>(sinv + srow * half + pair0));
       }
-      ov[v] = f32_to_bf16x8(f[j]);
+      const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+      const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
+      uint4 yo;
+      __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&yo);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        float a, b;
+        f2_unpack(f2_mul(f2_pack(f[2 * p], f[2 * p + 1]), rr), a, b);
+        const float2 yb = __bfloat1622float2(__floats2bfloat162_rn(a, b));
+        float ye, yo_;
+        f2_unpack(f2_mul(f2_pack(yb.x, yb.y), f2_pack(wf[2 * p], wf[2 * p + 1])), ye, yo_);
+        if (ROPE) {
+          float e, o;
+          f2_unpack(f2_add(f2_mul(f2_pack(ye, yo_), f2_pack(cc[p], cc[p])),
+                           f2_mul(f2_pack(yo_, ye), f2_pack(-ss[p], ss[p]))),
+                    e, o);
+          y2[p] = __floats2bfloat162_rn(e, o);
+        } else {
+          y2[p] = __floats2bfloat162_rn(ye, yo_);
+        }
+      }
+      ov[v] = yo;
     }
   }
 }
 
 static inline unsigned row_grid(int64_t rows) { return (unsigned)((rows + 7) / 8); }
+
+// Row kernels keep ceil(D / 256) 16-byte vectors per lane in registers; instantiate the
+// count for the row length (D <= 2048).
+template <typename F>
+static void dispatch_nv(int64_t D, F&& f) {
+  if (D <= 512) f(std::integral_constant<int, 2>{});
+  else if (D <= 1024) f(std::integral_constant<int, 4>{});
+  else if (D <= 1536) f(std::integral_constant<int, 6>{});
+  else f(std::integral_constant<int, 8>{});
+}
 
 }  // namespace fvb
 
@@ -266,30 +346,40 @@ int fvb_ln_modulate(const void* x, const void* scale, const void* shift, int64_t
   FVB_REQUIRE(x && scale && shift && out, "fvb_ln_modulate: NULL pointer");
   FVB_REQUIRE(aligned16(x) && aligned16(scale) && aligned16(shift) && aligned16(out),
               "fvb_ln_modulate: pointers must be 16-byte aligned");
-  if (q8) {
-    FVB_REQUIRE((reinterpret_cast<uintptr_t>(q8) & 7u) == 0, "fvb_ln_modulate: q8 alignment");
-    ln_modulate_kernel<true><<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)scale, (const __nv_bfloat16*)shift, rows, L,
-        (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
-  } else {
-    ln_modulate_kernel<false><<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)scale, (const __nv_bfloat16*)shift, rows, L,
-        (int)D, eps, (__nv_bfloat16*)out, nullptr, nullptr);
-  }
+  if (q8) FVB_REQUIRE((reinterpret_cast<uintptr_t>(q8) & 7u) == 0, "fvb_ln_modulate: q8 alignment");
+  auto launch = [&](auto emit, auto nv) {
+    ln_modulate_kernel<decltype(emit)::value, decltype(nv)::value>
+        <<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
+            (const __nv_bfloat16*)x, (const __nv_bfloat16*)scale, (const __nv_bfloat16*)shift,
+            rows, L, (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
+  };
+  dispatch_nv(D, [&](auto nv) {
+    if (q8) launch(std::true_type{}, nv);
+    else launch(std::false_type{}, nv);
+  });
   return check_launch("fvb_ln_modulate");
 }
 
 int fvb_layer_norm(const void* x, const void* w, const void* b, int64_t rows, int64_t D,
-                   float eps, void* out, fvb_stream_t stream) {
+                   float eps, void* out, void* q8, float* q_scale, fvb_stream_t stream) {
   using namespace fvb;
   FVB_REQUIRE(rows >= 0 && D > 0 && D % 8 == 0 && D <= 2048, "fvb_layer_norm: bad shape");
+  FVB_REQUIRE((q8 == nullptr) == (q_scale == nullptr), "fvb_layer_norm: q8/q_scale go together");
   if (rows == 0) return FVB_OK;
   FVB_REQUIRE(x && out, "fvb_layer_norm: NULL pointer");
   FVB_REQUIRE(aligned16(x) && aligned16(out) && (!w || aligned16(w)) && (!b || aligned16(b)),
               "fvb_layer_norm: pointers must be 16-byte aligned");
-  layer_norm_kernel<<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
-      (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (const __nv_bfloat16*)b, rows, (int)D, eps,
-      (__nv_bfloat16*)out);
+  if (q8) FVB_REQUIRE((reinterpret_cast<uintptr_t>(q8) & 7u) == 0, "fvb_layer_norm: q8 alignment");
+  auto launch = [&](auto emit, auto nv) {
+    layer_norm_kernel<decltype(emit)::value, decltype(nv)::value>
+        <<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
+            (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (const __nv_bfloat16*)b, rows,
+            (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
+  };
+  dispatch_nv(D, [&](auto nv) {
+    if (q8) launch(std::true_type{}, nv);
+    else launch(std::false_type{}, nv);
+  });
   return check_launch("fvb_layer_norm");
 }
 
@@ -327,14 +417,18 @@ int fvb_rms_rope(const void* x, int64_t x_ld, const void* w, const float* cos, c
     FVB_REQUIRE(head_dim > 0 && head_dim % 8 == 0 && D % head_dim == 0,
                 "fvb_rms_rope: head_dim must divide D and be a multiple of 8");
     FVB_REQUIRE(cos && sin && aligned16(cos) && aligned16(sin), "fvb_rms_rope: cos/sin");
-    rms_rope_kernel<true><<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16*)x, x_ld, (const __nv_bfloat16*)w, cos, sin, rows, L, (int)D,
-        (int)head_dim, eps, out_row_map, (__nv_bfloat16*)out);
-  } else {
-    rms_rope_kernel<false><<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16*)x, x_ld, (const __nv_bfloat16*)w, nullptr, nullptr, rows, L,
-        (int)D, head_dim > 0 ? (int)head_dim : 128, eps, out_row_map, (__nv_bfloat16*)out);
   }
+  const int hd = rope ? (int)head_dim : (head_dim > 0 ? (int)head_dim : 128);
+  auto launch = [&](auto r, auto nv) {
+    rms_rope_kernel<decltype(r)::value, decltype(nv)::value>
+        <<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
+            (const __nv_bfloat16*)x, x_ld, (const __nv_bfloat16*)w, rope ? cos : nullptr,
+            rope ? sin : nullptr, rows, L, (int)D, hd, eps, out_row_map, (__nv_bfloat16*)out);
+  };
+  dispatch_nv(D, [&](auto nv) {
+    if (rope) launch(std::true_type{}, nv);
+    else launch(std::false_type{}, nv);
+  });
   return check_launch("fvb_rms_rope");
 }
 

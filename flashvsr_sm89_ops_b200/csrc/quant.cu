@@ -35,9 +35,8 @@ __device__ __forceinline__ float quant_scale_from_amax(float amax) {
 
 __device__ __forceinline__ float clamp448(float v) { return fminf(fmaxf(v, -kFp8Max), kFp8Max); }
 
-// 8 values -> 8 e4m3 codes packed in a uint2
-__device__ __forceinline__ uint2 quant8(const float* f, float s) {
-  const float rs = __frcp_rn(s);
+// 8 values -> 8 e4m3 codes packed in a uint2; rs = __frcp_rn(s), hoisted by the caller
+__device__ __forceinline__ uint2 quant8(const float* f, float s, float rs) {
   uint32_t w[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -101,12 +100,13 @@ __global__ void __launch_bounds__(256) quant_tensor_kernel(
     float* __restrict__ scale_out) {
   const float amax = *amax_p;
   const float s = quant_scale_from_amax(amax);
+  const float rs = __frcp_rn(s);
   if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = __fdiv_rn(amax, kFp8Max);
   for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
        v += (int64_t)gridDim.x * blockDim.x) {
     float f[8];
     load8<GELU>(x, v, f);
-    q[v] = quant8(f, s);
+    q[v] = quant8(f, s, rs);
   }
   if (blockIdx.x == 0) {
     for (int64_t i = nvec * 8 + threadIdx.x; i < n; i += blockDim.x) {
@@ -147,10 +147,11 @@ __global__ void __launch_bounds__(256) quant_row_kernel(const __nv_bfloat16* __r
     }
     m = warp_max(m);
     const float s = quant_scale_from_amax(m);
+    const float rs = __frcp_rn(s);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       int64_t v = (int64_t)j * 32 + lane;
-      if (v < nvec) qv[v] = quant8(f[j], s);
+      if (v < nvec) qv[v] = quant8(f[j], s, rs);
     }
   } else {
     for (int64_t v = lane; v < nvec; v += 32) {
@@ -161,29 +162,48 @@ __global__ void __launch_bounds__(256) quant_row_kernel(const __nv_bfloat16* __r
     }
     m = warp_max(m);
     const float s = quant_scale_from_amax(m);
+    const float rs = __frcp_rn(s);
     for (int64_t v = lane; v < nvec; v += 32) {
       float f[8];
       load8<GELU>(xv, v, f);
-      qv[v] = quant8(f, s);
+      qv[v] = quant8(f, s, rs);
     }
   }
   if (lane == 0) scale_out[row] = __fdiv_rn(m, kFp8Max);
 }
 
 // quantise with a known amax ([1] per-tensor or [M] per-row); flat, vectorised
+// Rows are dealt to blocks; the scale and its reciprocal are computed once per row and
+// each thread keeps four 16-byte loads in flight.  (A flat grid-stride loop over the
+// whole matrix spent more time in its 64-bit row = v / (K/8) divides than in memory.)
 __global__ void __launch_bounds__(256) quant_with_amax_kernel(
     const uint4* __restrict__ g, int64_t M, int64_t K, const float* __restrict__ amax, int per_row,
     uint2* __restrict__ q, float* __restrict__ scale_out) {
-  const int64_t kv = K >> 3;
-  const int64_t nvec = M * kv;
-  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
-       v += (int64_t)gridDim.x * blockDim.x) {
-    int64_t row = per_row ? v / kv : 0;
-    float a = __ldg(amax + row);
-    float f[8];
-    bf16x8_to_f32(__ldg(g + v), f);
-    q[v] = quant8(f, quant_scale_from_amax(a));
-    if (per_row ? (v % kv == 0) : (v == 0)) scale_out[row] = __fdiv_rn(a, kFp8Max);
+  const int kv = (int)(K >> 3);  // vectors per row (K < 2^34 enforced by the host)
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const float a = __ldg(amax + (per_row ? row : 0));
+    const float s = quant_scale_from_amax(a);
+    const float rs = __frcp_rn(s);
+    if (threadIdx.x == 0 && (per_row || row == 0)) scale_out[per_row ? row : 0] = __fdiv_rn(a, kFp8Max);
+    const uint4* gr = g + row * kv;
+    uint2* qr = q + row * kv;
+    int v = threadIdx.x;
+    for (; v + 3 * 256 < kv; v += 4 * 256) {
+      uint4 u[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) u[t] = __ldg(gr + v + t * 256);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float f[8];
+        bf16x8_to_f32(u[t], f);
+        qr[v + t * 256] = quant8(f, s, rs);
+      }
+    }
+    for (; v < kv; v += 256) {
+      float f[8];
+      bf16x8_to_f32(__ldg(gr + v), f);
+      qr[v] = quant8(f, s, rs);
+    }
   }
 }
 
@@ -269,8 +289,9 @@ int fvb_quant_fp8_with_amax(const void* g, int64_t M, int64_t K, const float* am
   FVB_REQUIRE(K % 8 == 0, "fvb_quant_fp8_with_amax: K %% 8 != 0");
   FVB_REQUIRE(aligned16(g) && (reinterpret_cast<uintptr_t>(q) & 7u) == 0,
               "fvb_quant_fp8_with_amax: misaligned pointer");
-  const int64_t nvec = M * K / 8;
-  quant_with_amax_kernel<<<grid_for(nvec, 256), 256, 0, (cudaStream_t)stream>>>(
+  FVB_REQUIRE(K / 8 <= 0x7fffffff, "fvb_quant_fp8_with_amax: row too long");
+  const int64_t rows_grid = M < (int64_t)sm_count() * 8 ? M : (int64_t)sm_count() * 8;
+  quant_with_amax_kernel<<<(unsigned)rows_grid, 256, 0, (cudaStream_t)stream>>>(
       (const uint4*)g, M, K, amax, mode == FVB_SCALE_ROW, (uint2*)q, scale_out);
   return check_launch("fvb_quant_fp8_with_amax");
 }

@@ -59,8 +59,12 @@ def fused_gate_add(x: torch.Tensor, gate: torch.Tensor | None, residual: torch.T
 
 
 def layer_norm(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None,
-               eps: float = 1e-6, out: torch.Tensor | None = None):
-    """torch.nn.LayerNorm semantics (fp32 math, one bf16 rounding) over the last dim."""
+               eps: float = 1e-6, out: torch.Tensor | None = None, emit_fp8: bool = False):
+    """torch.nn.LayerNorm semantics (fp32 math, one bf16 rounding) over the last dim.
+
+    emit_fp8=True also returns the output's per-token FP8 codes [rows, D] and scales [rows]
+    (what quantize_fp8(out, "token") gives), computed in the same pass:
+    returns (out, q8, scale)."""
     _check(x, "layer_norm")
     D = x.shape[-1]
     x = x.contiguous()
@@ -69,6 +73,12 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor 
     b = bias.to(torch.bfloat16).contiguous() if bias is not None else None
     if out is None:
         out = torch.empty_like(x)
+    q8 = qs = None
+    if emit_fp8:
+        q8 = torch.empty((rows, D), dtype=torch.float8_e4m3fn, device=x.device)
+        qs = torch.empty((rows,), dtype=torch.float32, device=x.device)
     _lib.call("fvb_layer_norm", _lib.ptr(x), _lib.ptr(w), _lib.ptr(b), rows, D, float(eps),
-              _lib.ptr(out), _lib.stream_of(x))
+              _lib.ptr(out), _lib.ptr(q8), _lib.ptr(qs), _lib.stream_of(x))
+    if emit_fp8:
+        return out, q8, qs
     return out

@@ -291,8 +291,16 @@ def _make_dit_block_forward(dit):
             x = self.gate(x, gate_msa, self_attn_output)
         if fast:
             n3 = _unwrap(self.norm3)
-            xn = layer_norm(x, n3.weight, n3.bias, eps=getattr(n3, "eps", 1e-6))
-            x = fused_gate_add(x, None, self.cross_attn(xn, context, is_stream=is_stream))
+            ca = self.cross_attn
+            if token and type(getattr(ca, "q", None)) is FP8Linear and ca.q.mode == "token":
+                # norm3 also emits the per-token FP8 codes of its output: the cross-attention
+                # q projection takes them instead of quantising xn again
+                xn, x8, s8 = layer_norm(x, n3.weight, n3.bias, eps=getattr(n3, "eps", 1e-6),
+                                        emit_fp8=True)
+                ca._fvb_x8 = (xn, x8, s8)
+            else:
+                xn = layer_norm(x, n3.weight, n3.bias, eps=getattr(n3, "eps", 1e-6))
+            x = fused_gate_add(x, None, ca(xn, context, is_stream=is_stream))
         else:
             x = x + self.cross_attn(self.norm3(x), context, is_stream=is_stream)
         if fa is not None:

@@ -146,10 +146,15 @@ FVB_API int fvb_ln_modulate(const void* x, const void* scale, const void* shift,
                     int64_t D, float eps, void* out, void* q8, float* q_scale,
                     fvb_stream_t stream);
 
-/* LayerNorm with affine weight/bias (the block's norm3; not fused in the reference):
- *   out = bf16( bf16((x-mean)/sqrt(var+eps)) * w + b )   (w, b [D] bf16; b may be NULL) */
+/* LayerNorm with affine weight/bias (the block's norm3: torch.nn.LayerNorm on bf16, which the
+ * reference leaves to PyTorch, wan_video_dit DiTBlock.norm3):
+ *   out = bf16( (x-mean)/sqrt(var+eps) * w + b )   fp32 math, one rounding
+ *   (w, b [D] bf16; either may be NULL).
+ * q8/q_scale (optional, both or neither): also emit out's per-token FP8 E4M3 codes and scales
+ * exactly as fvb_quant_fp8(out, FVB_SCALE_ROW) would (the cross-attention q projection's
+ * input quantisation, fp8_linear.py:60-66, done in the same pass). */
 FVB_API int fvb_layer_norm(const void* x, const void* w, const void* b, int64_t rows, int64_t D,
-                   float eps, void* out, fvb_stream_t stream);
+                   float eps, void* out, void* q8, float* q_scale, fvb_stream_t stream);
 
 /* ------------------------------------------------- a9: gated residual
  * Replaces fused_gate_add(x, gate, residual) (fused_adaln.py:74-85; kernel :45-57):

@@ -122,16 +122,23 @@ def test_ln_modulate(B, L, D):
     assert torch.equal(q8.view(torch.uint8), qq.view(torch.uint8)) and torch.equal(qs, ss)
 
 
-def test_layer_norm_affine():
+@pytest.mark.parametrize("L,D,with_bias", [(4224, 1536, True), (37, 256, False)])
+def test_layer_norm_affine(L, D, with_bias):
+    from flashvsr_sm89_ops_b200 import quantize_fp8
     from flashvsr_sm89_ops_b200.fused_adaln import layer_norm
-    x = torch.randn(1, 4224, 1536, generator=gen(6)).to(torch.bfloat16)
-    w = (1 + 0.1 * torch.randn(1536, generator=gen(7))).to(torch.bfloat16)
-    b = (0.1 * torch.randn(1536, generator=gen(8))).to(torch.bfloat16)
-    out = layer_norm(x.to(DEV), w.to(DEV), b.to(DEV))
+    x = torch.randn(1, L, D, generator=gen(6)).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(D, generator=gen(7))).to(torch.bfloat16)
+    b = (0.1 * torch.randn(D, generator=gen(8))).to(torch.bfloat16) if with_bias else None
+    out = layer_norm(x.to(DEV), w.to(DEV), None if b is None else b.to(DEV))
     xf = x.float()
     xn = (xf - xf.mean(-1, keepdim=True)) / torch.sqrt(xf.var(-1, unbiased=False, keepdim=True) + 1e-6)
     ok, frac, dmax = within_ulps(out, O.layer_norm(x, w, b), xn * w.float())
     assert ok and frac < 1e-2, (frac, dmax)
+    # the FP8 emission equals quantising the bf16 output per token
+    out2, q8, qs = layer_norm(x.to(DEV), w.to(DEV), None if b is None else b.to(DEV), emit_fp8=True)
+    assert torch.equal(out2, out)
+    qq, ss = quantize_fp8(out.reshape(-1, D), "token")
+    assert torch.equal(q8.view(torch.uint8), qq.view(torch.uint8)) and torch.equal(qs, ss)
 
 
 # ----------------------------------------------------------------------------- RMS+RoPE
