@@ -329,11 +329,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 // window costs 64 KB of L2 -> shared memory traffic per 8.4 MFLOP, and the kernel runs
 // within ~20% of a copy of itself that only performs those loads.
 // TMEM: S [0,128), P_A [128,192), P_B [192,256), O_A [256,384), O_B [384,512).
-// MMA order: S_A0 S_B0 S_A1 | PV_A(j) S_B(j+1) PV_B(j) S_A(j+2) | ...; loads follow it.
+// Each item has its own TMA warp and MMA-issuing warp: one thread issuing for both items
+// was the critical path (its per-operation overhead showed up one for one in the
+// kernel's time).
 // ===========================================================================
 namespace bsa6 {
 
-constexpr int kThreads = 320;  // warps 0-7 softmax (item = warp/4), 8 TMA, 9 MMA
+// warps 0-7 softmax (item = warp/4); per item x: warp 8+x loads its tiles, warp 10+x
+// issues its MMAs.  The items' pipelines meet only in the shared S buffer.
+constexpr int kThreads = 384;
 constexpr int kTile = 128;
 constexpr int kAtom = 128 * 128;
 constexpr int kTileBytes = 2 * kAtom;
@@ -406,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == 10) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -417,66 +421,78 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int col_q = h * kTile;
   const int jmax = it[0].cnt > it[1].cnt ? it[0].cnt : it[1].cnt;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && jmax > 0) {
+  if (warp == 8 || warp == 9) {
+    // ------------------------------------------------------------ TMA producer of item x
+    const int x = warp - 8;
+    const Item me = x ? it[1] : it[0];
+    if (lane == 0 && me.cnt > 0) {
+      uint8_t* const q_s = x ? sQ[1] : sQ[0];
+      uint8_t* const k_s = x ? sK[1] : sK[0];
+      uint8_t* const v_s = x ? sV[1] : sV[0];
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
       bool ok = true;
-      auto load_k = [&](int x, int j) {
-        if (!ok || j >= it[x].cnt) return;
-        if (!mbar_wait(BAR(x, K_EMPTY), (uint32_t)(j & 1) ^ 1u, 0x701u)) { ok = false; return; }
-        const int krow = __ldg(it[x].sel + j) * kTile;
-        mbar_arrive_expect_tx(BAR(x, K_FULL), kTileBytes);
-        tma_load_2d(sK[x], &tmK, BAR(x, K_FULL), col_q, krow);
-        tma_load_2d(sK[x] + kAtom, &tmK, BAR(x, K_FULL), col_q + 64, krow);
-      };
-      auto load_v = [&](int x, int j) {
-        if (!ok || j >= it[x].cnt) return;
-        if (!mbar_wait(BAR(x, V_EMPTY), (uint32_t)(j & 1) ^ 1u, 0x702u)) { ok = false; return; }
-        const int krow = __ldg(it[x].sel + j) * kTile;
-        mbar_arrive_expect_tx(BAR(x, V_FULL), kTileBytes);
-        tma_load_2d(sV[x], &tmV, BAR(x, V_FULL), col_q, krow);
-        tma_load_2d(sV[x] + kAtom, &tmV, BAR(x, V_FULL), col_q + 64, krow);
-      };
-#pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        if (it[x].cnt > 0) {
-          mbar_arrive_expect_tx(BAR(x, Q_FULL), kTileBytes);
-          tma_load_2d(sQ[x], &tmQ, BAR(x, Q_FULL), col_q, it[x].qb * kTile);
-          tma_load_2d(sQ[x] + kAtom, &tmQ, BAR(x, Q_FULL), col_q + 64, it[x].qb * kTile);
+      mbar_arrive_expect_tx(BAR(x, Q_FULL), kTileBytes);
+      tma_load_2d(q_s, &tmQ, BAR(x, Q_FULL), col_q, me.qb * kTile);
+      tma_load_2d(q_s + kAtom, &tmQ, BAR(x, Q_FULL), col_q + 64, me.qb * kTile);
+      // The item's MMA warp consumes K(0) K(1) V(0) K(2) V(1) ...; K(j) waits until S(j-1)
+      // has read the K slot, V(j) until P.V(j-1) has read the V slot.
+      for (int j = 0; j <= me.cnt && ok; ++j) {
+        if (j < me.cnt) {
+          const int krow = __ldg(me.sel + j) * kTile;
+          if (!mbar_wait(BAR(x, K_EMPTY), (uint32_t)(j & 1) ^ 1u, 0x701u)) { ok = false; break; }
+          mbar_arrive_expect_tx(BAR(x, K_FULL), kTileBytes);
+          tma_load_2d(k_s, &tmK, BAR(x, K_FULL), col_q, krow);
+          tma_load_2d(k_s + kAtom, &tmK, BAR(x, K_FULL), col_q + 64, krow);
         }
-      }
-      // same order as the MMA warp consumes them
-      load_k(0, 0);
-      load_k(1, 0);
-      for (int j = 0; j < jmax && ok; ++j) {
-        load_k(0, j + 1);
-        load_v(0, j);
-        load_k(1, j + 1);
-        load_v(1, j);
+        if (j >= 1) {
+          const int jv = j - 1;
+          const int vrow = __ldg(me.sel + jv) * kTile;
+          if (!mbar_wait(BAR(x, V_EMPTY), (uint32_t)(jv & 1) ^ 1u, 0x702u)) { ok = false; break; }
+          mbar_arrive_expect_tx(BAR(x, V_FULL), kTileBytes);
+          tma_load_2d(v_s, &tmV, BAR(x, V_FULL), col_q, vrow);
+          tma_load_2d(v_s + kAtom, &tmV, BAR(x, V_FULL), col_q + 64, vrow);
+        }
       }
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && jmax > 0) {
+  } else if (warp == 10 || warp == 11) {
+    // ------------------------------------------------------------ MMA issuer of item x
+    const int x = warp - 10;
+    const Item me = x ? it[1] : it[0];
+    const int other_cnt = x ? it[0].cnt : it[1].cnt;
+    if (lane == 0 && me.cnt > 0) {
       constexpr uint32_t idesc_s = make_idesc(1 /*bf16*/, 1 /*bf16*/, 0, 0, 128, 128);
       constexpr uint32_t idesc_o = make_idesc(1, 1, 0 /*P K-major*/, 1 /*V MN-major*/, 128, 128);
+      const uint32_t q0 = smem_u32(x ? sQ[1] : sQ[0]);
+      const uint32_t k0 = smem_u32(x ? sK[1] : sK[0]);
+      const uint32_t v0 = smem_u32(x ? sV[1] : sV[0]);
+      const uint32_t tP = tmem + kColP + (uint32_t)(x * 64);
+      const uint32_t tO = tmem + kColO + (uint32_t)(x * 128);
+      uint64_t* const free_mine = BAR(x, S_FREE);
+      uint64_t* const free_other = BAR(x ^ 1, S_FREE);
       bool ok = true;
-      int last_x = -1, last_j = 0;  // owner of the S buffer's current contents
-      auto issue_s = [&](int x, int j) {
-        if (!ok || j >= it[x].cnt) return;
+      // The S buffer holds S_A(0) S_B(0) S_A(1) S_B(1) ... in turn (an item past its count
+      // drops out): S_x(j) waits until the softmax of the previous occupant copied it out.
+      // previous occupant of S_A(j): S_B(j-1) if B reached j-1, else S_A(j-1);
+      // of S_B(j): S_A(j) if A reaches j, else S_B(j-1).
+      auto issue_s = [&](int j) {
+        if (!ok || j >= me.cnt) return;
         if (j == 0 && !mbar_wait(BAR(x, Q_FULL), 0, 0x703u)) { ok = false; return; }
-        // the previous S in the shared buffer must have been copied out by its softmax
-        if (last_x >= 0 && !mbar_wait(BAR(last_x, S_FREE), (uint32_t)(last_j & 1), 0x704u)) {
-          ok = false;
-          return;
+        bool w = true;
+        if (x == 0) {
+          if (j >= 1)
+            w = (j - 1 < other_cnt) ? mbar_wait(free_other, (uint32_t)((j - 1) & 1), 0x704u)
+                                    : mbar_wait(free_mine, (uint32_t)((j - 1) & 1), 0x704u);
+        } else {
+          if (j < other_cnt)
+            w = mbar_wait(free_other, (uint32_t)(j & 1), 0x704u);
+          else if (j >= 1)
+            w = mbar_wait(free_mine, (uint32_t)((j - 1) & 1), 0x704u);
         }
+        if (!w) { ok = false; return; }
         if (!mbar_wait(BAR(x, K_FULL), (uint32_t)(j & 1), 0x705u)) { ok = false; return; }
         tc_fence_after();
-        const uint32_t q0 = smem_u32(sQ[x]);
-        const uint32_t k0 = smem_u32(sK[x]);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (uint32_t)((kk >> 2) * kAtom + (kk & 3) * 32);
@@ -485,17 +501,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_commit(BAR(x, S_FULL));
         tc_commit(BAR(x, K_EMPTY));
-        last_x = x;
-        last_j = j;
       };
-      auto issue_pv = [&](int x, int j) {
-        if (!ok || j >= it[x].cnt) return;
+      auto issue_pv = [&](int j) {
+        if (!ok || j >= me.cnt) return;
         if (!mbar_wait(BAR(x, P_FULL), (uint32_t)(j & 1), 0x706u)) { ok = false; return; }
         if (!mbar_wait(BAR(x, V_FULL), (uint32_t)(j & 1), 0x707u)) { ok = false; return; }
         tc_fence_after();
-        const uint32_t v0 = smem_u32(sV[x]);
-        const uint32_t tP = tmem + kColP + (uint32_t)(x * 64);
-        const uint32_t tO = tmem + kColO + (uint32_t)(x * 128);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           // keys [16kk, 16kk+16) are P columns [8kk, 8kk+8)
@@ -506,14 +517,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit(BAR(x, V_EMPTY));
         tc_commit(BAR(x, PV_DONE));
       };
-      issue_s(0, 0);
-      issue_s(1, 0);
-      issue_s(0, 1);
-      for (int j = 0; j < jmax && ok; ++j) {
-        issue_pv(0, j);
-        issue_s(1, j + 1);
-        issue_pv(1, j);
-        issue_s(0, j + 2);
+      issue_s(0);
+      issue_s(1);
+      for (int j = 0; j < me.cnt && ok; ++j) {
+        issue_pv(j);
+        issue_s(j + 2);
       }
     }
   } else {
@@ -641,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 10) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

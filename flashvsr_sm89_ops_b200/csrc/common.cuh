@@ -124,6 +124,29 @@ __device__ __forceinline__ uint4 f32_to_bf16x8(const float* f) {
 }
 
 // ---------------------------------------------------------------------------
+// row kernels (one warp per row of a row-major matrix)
+// ---------------------------------------------------------------------------
+// Rows are dealt to warps round-robin over a grid of at most 3 blocks per SM; each warp
+// loads its next row while it works on the current one, so two rows per warp are in flight
+// (one row per warp, load -> reduce -> store in series, left HBM idle between phases).
+constexpr int kRowBlocksPerSM = 3;
+
+template <int NV, typename Load, typename Body>
+__device__ __forceinline__ void row_pipeline(int64_t rows, Load load, Body body) {
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  uint4 cur[NV], nxt[NV];
+  load(row, cur);
+  for (; row < rows; row += nwarps) {
+    if (row + nwarps < rows) load(row + nwarps, nxt);
+    body(row, cur);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) cur[j] = nxt[j];
+  }
+}
+
+// ---------------------------------------------------------------------------
 // shared-memory / mbarrier PTX
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

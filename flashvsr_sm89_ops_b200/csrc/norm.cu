@@ -85,135 +85,132 @@ __device__ __forceinline__ void row_stats(const uint4* xr, int lane, int nvec, i
 // the exact result once, which is the same value (fp32 carries more than twice bf16's
 // precision plus two bits, so the fp32 intermediate never changes a bf16 rounding).
 template <bool EMIT_FP8, int NV>
-__global__ void __launch_bounds__(256) ln_modulate_kernel(
+__global__ void __launch_bounds__(256, kRowBlocksPerSM) ln_modulate_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ scale,
     const __nv_bfloat16* __restrict__ shift, int64_t rows, int64_t L, int D, float eps,
     __nv_bfloat16* __restrict__ out, uint8_t* __restrict__ q8, float* __restrict__ q_scale) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
   const int nvec = D >> 3;
-  const int64_t b = row / L;
-  const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
-  const uint4* sv = reinterpret_cast<const uint4*>(scale + b * D);
-  const uint4* hv = reinterpret_cast<const uint4*>(shift + b * D);
-  uint4 xr[NV], sr[NV], hr[NV];
+  auto load = [&](int64_t row, uint4* xr) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int v = j * 32 + lane;
-    if (v < nvec) {
-      xr[j] = __ldg(xv + v);
-      sr[j] = __ldg(sv + v);
-      hr[j] = __ldg(hv + v);
-    }
-  }
-  float mean, rden;
-  row_stats<NV>(xr, lane, nvec, D, eps, mean, rden);
-  const uint64_t nm = f2_pack(-mean, -mean), rd = f2_pack(rden, rden);
-  const __nv_bfloat162 one2 = __float2bfloat162_rn(1.0f);
-  __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
-  uint4* ov = reinterpret_cast<uint4*>(out + row * D);
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int v = j * 32 + lane;
-    if (v < nvec) {
-      float f[8];
-      bf16x8_to_f32(xr[j], f);
-      const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&sr[j]);
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&hr[j]);
-      uint4 yo;
-      __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&yo);
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        float a, c;
-        f2_unpack(f2_mul(f2_add(f2_pack(f[2 * p], f[2 * p + 1]), nm), rd), a, c);
-        const __nv_bfloat162 xn = __floats2bfloat162_rn(a, c);
-        // _rn forms: no contraction of the multiply and the add into one bf16 fma
-        const __nv_bfloat162 y = __hadd2_rn(__hmul2_rn(xn, __hadd2_rn(one2, s2[p])), h2[p]);
-        y2[p] = y;
-        if (EMIT_FP8) m2 = __hmax2(m2, __habs2(y));
-      }
-      ov[v] = yo;
-      xr[j] = yo;
-    }
-  }
-  if (EMIT_FP8) {
-    const float2 mf = __bfloat1622float2(m2);
-    const float amax = warp_max(fmaxf(mf.x, mf.y));
-    const float qs = quant_scale_from_amax_n(amax);
-    const float rqs = __frcp_rn(qs);
-    uint2* qv = reinterpret_cast<uint2*>(q8 + row * D);
+    for (int j = 0; j < NV; ++j)
+      if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+  };
+  auto body = [&](int64_t row, uint4* xr) {
+    const int64_t b = row / L;
+    // scale / shift rows are shared by all rows of a batch item: L1 hits after the first
+    const uint4* sv = reinterpret_cast<const uint4*>(scale + b * D);
+    const uint4* hv = reinterpret_cast<const uint4*>(shift + b * D);
+    float mean, rden;
+    row_stats<NV>(xr, lane, nvec, D, eps, mean, rden);
+    const uint64_t nm = f2_pack(-mean, -mean), rd = f2_pack(rden, rden);
+    const __nv_bfloat162 one2 = __float2bfloat162_rn(1.0f);
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
+    uint4* ov = reinterpret_cast<uint4*>(out + row * D);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int v = j * 32 + lane;
-      if (v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
+      if (v < nvec) {
+        float f[8];
+        bf16x8_to_f32(xr[j], f);
+        const uint4 su = __ldg(sv + v), hu = __ldg(hv + v);
+        const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&su);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&hu);
+        uint4 yo;
+        __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&yo);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          float a, c;
+          f2_unpack(f2_mul(f2_add(f2_pack(f[2 * p], f[2 * p + 1]), nm), rd), a, c);
+          const __nv_bfloat162 xn = __floats2bfloat162_rn(a, c);
+          // _rn forms: no contraction of the multiply and the add into one bf16 fma
+          const __nv_bfloat162 y = __hadd2_rn(__hmul2_rn(xn, __hadd2_rn(one2, s2[p])), h2[p]);
+          y2[p] = y;
+          if (EMIT_FP8) m2 = __hmax2(m2, __habs2(y));
+        }
+        ov[v] = yo;
+        xr[j] = yo;
+      }
     }
-    if (lane == 0) q_scale[row] = __fdiv_rn(amax, 448.0f);
-  }
+    if (EMIT_FP8) {
+      const float2 mf = __bfloat1622float2(m2);
+      const float amax = warp_max(fmaxf(mf.x, mf.y));
+      const float qs = quant_scale_from_amax_n(amax);
+      const float rqs = __frcp_rn(qs);
+      uint2* qv = reinterpret_cast<uint2*>(q8 + row * D);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int v = j * 32 + lane;
+        if (v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
+      }
+      if (lane == 0) q_scale[row] = __fdiv_rn(amax, 448.0f);
+    }
+  };
+  row_pipeline<NV>(rows, load, body);
 }
 
 // LayerNorm with optional affine weight / bias, fp32 math and one bf16 rounding (the
 // semantics of torch.nn.LayerNorm on bf16 tensors); optionally also the per-token e4m3
 // codes of that bf16 output (what the next FP8 linear would compute from it).
 template <bool EMIT_FP8, int NV>
-__global__ void __launch_bounds__(256) layer_norm_kernel(const __nv_bfloat16* __restrict__ x,
-                                                          const __nv_bfloat16* __restrict__ w,
-                                                          const __nv_bfloat16* __restrict__ bias,
-                                                          int64_t rows, int D, float eps,
-                                                          __nv_bfloat16* __restrict__ out,
-                                                          uint8_t* __restrict__ q8,
-                                                          float* __restrict__ q_scale) {
+__global__ void __launch_bounds__(256, 2) layer_norm_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+    const __nv_bfloat16* __restrict__ bias, int64_t rows, int D, float eps,
+    __nv_bfloat16* __restrict__ out, uint8_t* __restrict__ q8, float* __restrict__ q_scale) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
   const int nvec = D >> 3;
-  const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
-  uint4 xr[NV];
+  auto load = [&](int64_t row, uint4* xr) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
 #pragma unroll
-  for (int j = 0; j < NV; ++j)
-    if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
-  float mean, rstd;
-  row_stats<NV>(xr, lane, nvec, D, eps, mean, rstd);
-  float amax = 0.f;
-  uint4* ov = reinterpret_cast<uint4*>(out + row * D);
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int v = j * 32 + lane;
-    if (v < nvec) {
-      float f[8], ww[8], bb[8];
-      bf16x8_to_f32(xr[j], f);
-      if (w) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), ww);
-      if (bias) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(bias) + v), bb);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float y = (f[i] - mean) * rstd;
-        if (w) y = y * ww[i];
-        if (bias) y = y + bb[i];
-        f[i] = y;
-      }
-      const uint4 yo = f32_to_bf16x8(f);
-      ov[v] = yo;
-      if (EMIT_FP8) {
-        float r[8];
-        bf16x8_to_f32(yo, r);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(r[i]));
-        xr[j] = yo;
-      }
-    }
-  }
-  if (EMIT_FP8) {
-    amax = warp_max(amax);
-    const float qs = quant_scale_from_amax_n(amax);
-    const float rqs = __frcp_rn(qs);
-    uint2* qv = reinterpret_cast<uint2*>(q8 + row * D);
+    for (int j = 0; j < NV; ++j)
+      if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+  };
+  auto body = [&](int64_t row, uint4* xr) {
+    float mean, rstd;
+    row_stats<NV>(xr, lane, nvec, D, eps, mean, rstd);
+    float amax = 0.f;
+    uint4* ov = reinterpret_cast<uint4*>(out + row * D);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int v = j * 32 + lane;
-      if (v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
+      if (v < nvec) {
+        float f[8], ww[8], bb[8];
+        bf16x8_to_f32(xr[j], f);
+        if (w) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), ww);
+        if (bias) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(bias) + v), bb);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float y = (f[i] - mean) * rstd;
+          if (w) y = y * ww[i];
+          if (bias) y = y + bb[i];
+          f[i] = y;
+        }
+        const uint4 yo = f32_to_bf16x8(f);
+        ov[v] = yo;
+        if (EMIT_FP8) {
+          float r[8];
+          bf16x8_to_f32(yo, r);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(r[i]));
+          xr[j] = yo;
+        }
+      }
     }
-    if (lane == 0) q_scale[row] = __fdiv_rn(amax, 448.0f);
-  }
+    if (EMIT_FP8) {
+      amax = warp_max(amax);
+      const float qs = quant_scale_from_amax_n(amax);
+      const float rqs = __frcp_rn(qs);
+      uint2* qv = reinterpret_cast<uint2*>(q8 + row * D);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int v = j * 32 + lane;
+        if (v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
+      }
+      if (lane == 0) q_scale[row] = __fdiv_rn(amax, 448.0f);
+    }
+  };
+  row_pipeline<NV>(rows, load, body);
 }
 
 __global__ void __launch_bounds__(256) gate_add_kernel(const uint4* __restrict__ x,
@@ -244,81 +241,86 @@ __global__ void __launch_bounds__(256) gate_add_kernel(const uint4* __restrict__
 // bf16 values); the rotation rounds each product and the sum once, all in packed fp32 pairs
 // (mul.rn / add.rn per lane, no contraction), then one bf16 rounding.
 template <bool ROPE, int NV>
-__global__ void __launch_bounds__(256) rms_rope_kernel(
+__global__ void __launch_bounds__(256, kRowBlocksPerSM) rms_rope_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t x_ld, const __nv_bfloat16* __restrict__ w,
     const float* __restrict__ cosv, const float* __restrict__ sinv, int64_t rows, int64_t L,
     int D, int head_dim, float eps, const int32_t* __restrict__ row_map,
     __nv_bfloat16* __restrict__ out) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
   const int nvec = D >> 3;
-  const uint4* xv = reinterpret_cast<const uint4*>(x + row * x_ld);
-  uint4 xr[NV];
+  auto load = [&](int64_t row, uint4* xr) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x + row * x_ld);
 #pragma unroll
-  for (int j = 0; j < NV; ++j)
-    if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
-  uint64_t q2 = f2_pack(0.f, 0.f);
+    for (int j = 0; j < NV; ++j)
+      if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+  };
+  auto body = [&](int64_t row, uint4* xr) {
+    uint64_t q2 = f2_pack(0.f, 0.f);
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    if (j * 32 + lane < nvec) {
-      float f[8];
-      bf16x8_to_f32(xr[j], f);
+    for (int j = 0; j < NV; ++j) {
+      if (j * 32 + lane < nvec) {
+        float f[8];
+        bf16x8_to_f32(xr[j], f);
 #pragma unroll
-      for (int i = 0; i < 8; i += 2) {
-        const uint64_t t = f2_pack(f[i], f[i + 1]);
-        q2 = f2_fma(t, t, q2);
-      }
-    }
-  }
-  float qa, qb;
-  f2_unpack(q2, qa, qb);
-  const float rrms = __frsqrt_rn(__fdiv_rn(warp_sum(qa + qb), (float)D) + eps);
-  const uint64_t rr = f2_pack(rrms, rrms);
-  const int64_t srow = row % L;
-  const int half = head_dim >> 1;
-  const int64_t orow = row_map ? (int64_t)__ldg(row_map + row) : row;
-  uint4* ov = reinterpret_cast<uint4*>(out + orow * D);
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int v = j * 32 + lane;
-    if (v < nvec) {
-      float f[8], wf[8];
-      bf16x8_to_f32(xr[j], f);
-      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), wf);
-      float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f), s4 = c4;
-      if (ROPE) {
-        const int pair0 = ((v * 8) % head_dim) >> 1;  // 4 consecutive pairs
-        c4 = __ldg(reinterpret_cast<const float4*>(cosv + srow * half + pair0));
-        s4 = __ldg(reinterpret_cast<const float4*>(sinv + srow * half + pair0));
-      }
-      const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
-      const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
-      uint4 yo;
-      __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&yo);
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        float a, b;
-        f2_unpack(f2_mul(f2_pack(f[2 * p], f[2 * p + 1]), rr), a, b);
-        const float2 yb = __bfloat1622float2(__floats2bfloat162_rn(a, b));
-        float ye, yo_;
-        f2_unpack(f2_mul(f2_pack(yb.x, yb.y), f2_pack(wf[2 * p], wf[2 * p + 1])), ye, yo_);
-        if (ROPE) {
-          float e, o;
-          f2_unpack(f2_add(f2_mul(f2_pack(ye, yo_), f2_pack(cc[p], cc[p])),
-                           f2_mul(f2_pack(yo_, ye), f2_pack(-ss[p], ss[p]))),
-                    e, o);
-          y2[p] = __floats2bfloat162_rn(e, o);
-        } else {
-          y2[p] = __floats2bfloat162_rn(ye, yo_);
+        for (int i = 0; i < 8; i += 2) {
+          const uint64_t t = f2_pack(f[i], f[i + 1]);
+          q2 = f2_fma(t, t, q2);
         }
       }
-      ov[v] = yo;
     }
-  }
+    float qa, qb;
+    f2_unpack(q2, qa, qb);
+    const float rrms = __frsqrt_rn(__fdiv_rn(warp_sum(qa + qb), (float)D) + eps);
+    const uint64_t rr = f2_pack(rrms, rrms);
+    const int64_t srow = row % L;
+    const int half = head_dim >> 1;
+    const int64_t orow = row_map ? (int64_t)__ldg(row_map + row) : row;
+    uint4* ov = reinterpret_cast<uint4*>(out + orow * D);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int v = j * 32 + lane;
+      if (v < nvec) {
+        float f[8], wf[8];
+        bf16x8_to_f32(xr[j], f);
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), wf);
+        float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f), s4 = c4;
+        if (ROPE) {
+          const int pair0 = ((v * 8) % head_dim) >> 1;  // 4 consecutive pairs
+          c4 = __ldg(reinterpret_cast<const float4*>(cosv + srow * half + pair0));
+          s4 = __ldg(reinterpret_cast<const float4*>(sinv + srow * half + pair0));
+        }
+        const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+        const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
+        uint4 yo;
+        __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&yo);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          float a, b;
+          f2_unpack(f2_mul(f2_pack(f[2 * p], f[2 * p + 1]), rr), a, b);
+          const float2 yb = __bfloat1622float2(__floats2bfloat162_rn(a, b));
+          float ye, yo_;
+          f2_unpack(f2_mul(f2_pack(yb.x, yb.y), f2_pack(wf[2 * p], wf[2 * p + 1])), ye, yo_);
+          if (ROPE) {
+            float e, o;
+            f2_unpack(f2_add(f2_mul(f2_pack(ye, yo_), f2_pack(cc[p], cc[p])),
+                             f2_mul(f2_pack(yo_, ye), f2_pack(-ss[p], ss[p]))),
+                      e, o);
+            y2[p] = __floats2bfloat162_rn(e, o);
+          } else {
+            y2[p] = __floats2bfloat162_rn(ye, yo_);
+          }
+        }
+        ov[v] = yo;
+      }
+    }
+  };
+  row_pipeline<NV>(rows, load, body);
 }
 
-static inline unsigned row_grid(int64_t rows) { return (unsigned)((rows + 7) / 8); }
+static inline unsigned row_grid(int64_t rows, int blocks_per_sm = kRowBlocksPerSM) {
+  const int64_t need = (rows + 7) / 8, cap = (int64_t)sm_count() * blocks_per_sm;
+  return (unsigned)(need < cap ? need : cap);
+}
 
 // Row kernels keep ceil(D / 256) 16-byte vectors per lane in registers; instantiate the
 // count for the row length (D <= 2048).
@@ -372,7 +374,7 @@ int fvb_layer_norm(const void* x, const void* w, const void* b, int64_t rows, in
   if (q8) FVB_REQUIRE((reinterpret_cast<uintptr_t>(q8) & 7u) == 0, "fvb_layer_norm: q8 alignment");
   auto launch = [&](auto emit, auto nv) {
     layer_norm_kernel<decltype(emit)::value, decltype(nv)::value>
-        <<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
+        <<<row_grid(rows, 2), 256, 0, (cudaStream_t)stream>>>(
             (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (const __nv_bfloat16*)b, rows,
             (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
   };

@@ -11,6 +11,8 @@
 // Layout: x [M, K] bf16 row-major.  Per-token mode gives each row its own
 // scale; rows are handled one warp each with 16-byte vector loads, the row
 // held in registers when K <= 2048 and re-read from L1/L2 otherwise.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace fvb {
@@ -120,59 +122,84 @@ __global__ void __launch_bounds__(256) quant_tensor_kernel(
 // ---------------------------------------------------------------------------
 // per-token: one warp per row
 // ---------------------------------------------------------------------------
+// K <= 2048: the row lives in registers (NV 16-byte vectors per lane), two rows per warp in
+// flight (row_pipeline).  GELU values are bf16-rounded, so they are stored back into the
+// row's bf16 registers losslessly between the amax and the quantisation passes.
 template <bool GELU, int NV>
-__global__ void __launch_bounds__(256) quant_row_kernel(const __nv_bfloat16* __restrict__ x,
-                                                         int64_t M, int64_t K,
-                                                         uint8_t* __restrict__ q,
-                                                         float* __restrict__ scale_out) {
+__global__ void __launch_bounds__(256, kRowBlocksPerSM) quant_row_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t M, int64_t K, uint8_t* __restrict__ q,
+    float* __restrict__ scale_out) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= M) return;
-  const __nv_bfloat16* xr = x + row * K;
-  uint8_t* qr = q + row * K;
-  const int64_t nvec = K >> 3;  // K % 8 == 0 enforced by the host
-  const uint4* xv = reinterpret_cast<const uint4*>(xr);
-  uint2* qv = reinterpret_cast<uint2*>(qr);
-  float m = 0.f;
-  if constexpr (NV > 0) {
-    float f[NV][8];
+  const int nvec = (int)(K >> 3);  // K % 8 == 0 enforced by the host
+  auto load = [&](int64_t row, uint4* xr) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x + row * K);
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+      if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+  };
+  auto body = [&](int64_t row, uint4* xr) {
+    float m = 0.f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      int64_t v = (int64_t)j * 32 + lane;
-      if (v < nvec) {
-        load8<GELU>(xv, v, f[j]);
+      if (j * 32 + lane < nvec) {
+        float f[8];
+        bf16x8_to_f32(xr[j], f);
+        if (GELU) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[j][i]));
+          for (int i = 0; i < 8; ++i) f[i] = gelu_tanh_bf16(f[i]);
+          xr[j] = f32_to_bf16x8(f);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
       }
     }
     m = warp_max(m);
     const float s = quant_scale_from_amax(m);
     const float rs = __frcp_rn(s);
+    uint2* qv = reinterpret_cast<uint2*>(q + row * K);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      int64_t v = (int64_t)j * 32 + lane;
-      if (v < nvec) qv[v] = quant8(f[j], s, rs);
+      if (j * 32 + lane < nvec) {
+        float f[8];
+        bf16x8_to_f32(xr[j], f);
+        qv[j * 32 + lane] = quant8(f, s, rs);
+      }
     }
-  } else {
-    for (int64_t v = lane; v < nvec; v += 32) {
-      float f[8];
-      load8<GELU>(xv, v, f);
+    if (lane == 0) scale_out[row] = __fdiv_rn(m, kFp8Max);
+  };
+  row_pipeline<NV>(M, load, body);
+}
+
+// K > 2048: the row is read twice (amax, then quantise), the second pass from L1/L2
+template <bool GELU>
+__global__ void __launch_bounds__(256) quant_row_long_kernel(const __nv_bfloat16* __restrict__ x,
+                                                             int64_t M, int64_t K,
+                                                             uint8_t* __restrict__ q,
+                                                             float* __restrict__ scale_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const uint4* xv = reinterpret_cast<const uint4*>(x + row * K);
+  uint2* qv = reinterpret_cast<uint2*>(q + row * K);
+  const int64_t nvec = K >> 3;
+  float m = 0.f;
+  for (int64_t v = lane; v < nvec; v += 32) {
+    float f[8];
+    load8<GELU>(xv, v, f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
-    }
-    m = warp_max(m);
-    const float s = quant_scale_from_amax(m);
-    const float rs = __frcp_rn(s);
-    for (int64_t v = lane; v < nvec; v += 32) {
-      float f[8];
-      load8<GELU>(xv, v, f);
-      qv[v] = quant8(f, s, rs);
-    }
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+  }
+  m = warp_max(m);
+  const float s = quant_scale_from_amax(m);
+  const float rs = __frcp_rn(s);
+  for (int64_t v = lane; v < nvec; v += 32) {
+    float f[8];
+    load8<GELU>(xv, v, f);
+    qv[v] = quant8(f, s, rs);
   }
   if (lane == 0) scale_out[row] = __fdiv_rn(m, kFp8Max);
 }
 
-// quantise with a known amax ([1] per-tensor or [M] per-row); flat, vectorised
 // Rows are dealt to blocks; the scale and its reciprocal are computed once per row and
 // each thread keeps four 16-byte loads in flight.  (A flat grid-stride loop over the
 // whole matrix spent more time in its 64-bit row = v / (K/8) divides than in memory.)
@@ -233,14 +260,22 @@ static int quant_impl(const void* x, int64_t M, int64_t K, void* q, float* scale
   if (mode == FVB_SCALE_ROW) {
     FVB_REQUIRE(K % 8 == 0, "%s: per-token mode needs K %% 8 == 0 (K=%lld)", name, (long long)K);
     FVB_REQUIRE((reinterpret_cast<uintptr_t>(q) & 7u) == 0, "%s: q not 8-byte aligned", name);
-    const int rows_per_block = 8;
-    dim3 grid((unsigned)((M + rows_per_block - 1) / rows_per_block));
-    if (K <= 2048)
-      quant_row_kernel<GELU, 8><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, M, K,
-                                                       (uint8_t*)q, scale_out);
-    else
-      quant_row_kernel<GELU, 0><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, M, K,
-                                                       (uint8_t*)q, scale_out);
+    const int64_t need = (M + 7) / 8;
+    if (K <= 2048) {
+      const int64_t cap = (int64_t)sm_count() * kRowBlocksPerSM;
+      const unsigned grid = (unsigned)(need < cap ? need : cap);
+      auto launch = [&](auto nv) {
+        quant_row_kernel<GELU, decltype(nv)::value><<<grid, 256, 0, st>>>(
+            (const __nv_bfloat16*)x, M, K, (uint8_t*)q, scale_out);
+      };
+      if (K <= 512) launch(std::integral_constant<int, 2>{});
+      else if (K <= 1024) launch(std::integral_constant<int, 4>{});
+      else if (K <= 1536) launch(std::integral_constant<int, 6>{});
+      else launch(std::integral_constant<int, 8>{});
+    } else {
+      quant_row_long_kernel<GELU><<<(unsigned)need, 256, 0, st>>>((const __nv_bfloat16*)x, M, K,
+                                                                   (uint8_t*)q, scale_out);
+    }
     return check_launch(name);
   }
   FVB_REQUIRE(workspace != nullptr, "%s: per-tensor mode needs a workspace", name);
