@@ -335,6 +335,59 @@ def run_reference(args, world, rank):
 
 
 # ----------------------------------------------------------------------------- B200 arm
+def tiled_4k(runner, world, rank, dev, dist_mod):
+    """4K tiled frames/s: the 3840x2048 canvas in 24 tiles of 896x768 (the survey's scaling
+    plan, plan_tiles(target=threshold=700_000)), tile i on rank i % world, each tile through
+    the DiT streaming schedule (one f=6 chunk + seven f=2 chunks = 20 latent frames -> 80
+    output frames) by TiledDiTPipe, blended on the rank's GPU and reduced to rank 0 by the
+    pack's own render_tiled.  Strong scaling: the canvas is fixed, ranks split the tiles.
+    The LQ video (85 frames) lives in pinned host memory and each tile's crop is copied in,
+    as the reference's render_tiled does.  Timed on the device (events around the whole
+    render, max over ranks) after a one-tile warm-up."""
+    from flashvsr_sm89_ops_b200.runner import TiledDiTPipe
+    from flashvsr_sm89_ops_b200.tiling import plan_tiles, render_tiled
+    W4, H4 = 3840, 2048
+    pipe = TiledDiTPipe(runner)
+    frames_in = 4 * pipe.latent_frames() + 5  # 85
+    g = torch.Generator(device=dev).manual_seed(13)
+    lq = torch.empty((3, frames_in, H4, W4), dtype=torch.bfloat16, pin_memory=True)
+    for fi in range(frames_in):  # per frame, to keep the device staging buffer small
+        lq[:, fi].copy_((torch.rand(3, H4, W4, generator=g, device=dev) * 2 - 1).to(torch.bfloat16))
+    tiles = plan_tiles(W4, H4, target=700_000, threshold=700_000)
+    x, y, w, h = tiles[0]
+    pipe(LQ_video=lq[:, :, y:y + h, x:x + w].to(dev), num_frames=frames_in, height=h, width=w)
+    pipe.tokens = 0
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist_mod.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(dev)
+    e0.record(stream)
+    out = render_tiled(pipe, lq, tile_target=700_000, tile_threshold=700_000, device=dev)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1), float(pipe.tokens)], device=dev, dtype=torch.float64)
+    if world > 1:
+        tok = t[1:2].clone()
+        dist_mod.all_reduce(t[0:1], op=dist_mod.ReduceOp.MAX)
+        dist_mod.all_reduce(tok, op=dist_mod.ReduceOp.SUM)
+        t[1] = tok[0]
+    ms, tokens = float(t[0].item()), float(t[1].item())
+    if rank != 0:
+        return None
+    n_out = int(out.shape[1])
+    return {
+        "fps": n_out / (ms / 1e3), "unit": "frames/s", "frames": n_out, "ms": ms,
+        "canvas": f"{W4}x{H4}", "input_frames": frames_in, "tiles": len(tiles),
+        "tile": f"{w}x{h}", "tiles_per_rank": -(-len(tiles) // world),
+        "dit_tokens_per_s": tokens / (ms / 1e3), "scaling": "strong",
+        "checksum": float(out.float().abs().sum().item()),
+        "schedule": "per tile: f=6 chunk + 7 f=2 chunks (KV cache of 3 time rows), 30 blocks; "
+                    "patch-embed / unpatchify are bf16 linears standing in for the LQ "
+                    "projection and VAE",
+    }
+
+
 def attention_roofline(runner, iters, stream):
     """Time the dominant kernel (block-sparse attention at the step's shape) with CUDA events."""
     from flashvsr_sm89_ops_b200 import lcsa
@@ -381,7 +434,7 @@ def run_b200(args, world, rank, local_rank):
     torch.cuda.set_device(dev)
     runner = StreamingDiT(num_layers=args.blocks, dim=D, heads=HEADS, ffn=FFN, height=H_PX,
                           width=W_PX, ctx_len=CTX, kv_len=KV_LEN, mask_rule="causal",
-                          seed=rank, device=dev)
+                          seed=0, device=dev)  # one model, replicated on every rank
     runner.prime()
     tokens = runner.tokens(2)
     x_static = runner.make_input(2)
@@ -458,6 +511,10 @@ def run_b200(args, world, rank, local_rank):
     peaks, peak_kind = load_peaks()
     achieved = att_flops / (att_ms / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops", 1590.0))
+    tiled = None
+    if os.environ.get("FVB_SKIP_TILED") != "1":
+        import torch.distributed as dist_mod
+        tiled = tiled_4k(runner, world, rank, dev, dist_mod)
     devs = _lib.device_error()
     if devs:
         raise RuntimeError(f"device error word set: {devs:#x}")
@@ -483,6 +540,8 @@ def run_b200(args, world, rank, local_rank):
                      "launch_ms": att_ms, "flops_per_launch": att_flops},
         "clocks": clocks,
     }
+    if tiled is not None:
+        line["tiled_4k"] = tiled
     if world == 1 and os.environ.get("FVB_SKIP_CPU_BASELINE") != "1":
         t_block, threads = cpu_block_sample(steps=1, warm=False)
         cpu_value = tokens / (t_block * args.blocks)
@@ -508,8 +567,18 @@ def main():
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
+        # NCCL prints its version on stdout at init; keep stdout for the one JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local_rank))
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     try:
         run_b200(args, world, rank, local_rank)
     finally:

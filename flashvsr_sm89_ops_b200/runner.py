@@ -95,3 +95,60 @@ class StreamingDiT:
             y = self.step(x_static)
         self.graph = (g, y)
         return g, y
+
+
+class TiledDiTPipe:
+    """Stand-in FlashVSR pipeline for ``render_tiled`` (the 4K tiled workload).
+
+    Per tile: the LQ crop [C, F, h, w] is patch-embedded (16x16 px x 4 frames per token, one
+    bf16 linear), run through the DiT's streaming schedule (integrate.py:51-54): one f=6
+    chunk, then f=2 chunks whose self-attention reads the KV caches of the last ``kv_len``
+    time rows, and each chunk's output is unpatchified back to frames (one bf16 linear).
+    The patch embedding and the decoder are plain linears standing in for the pipeline's
+    LQ projection and VAE, which are not part of this operator pack.  Returns
+    [3, 4 * (6 + 2 * n_steps), h, w] bf16 frames.
+    """
+
+    def __init__(self, runner: StreamingDiT, n_steps: int = 7, seed: int = 5):
+        self.r = runner
+        self.n_steps = n_steps
+        dev = runner.device
+        g = torch.Generator(device=dev).manual_seed(seed)
+        patch = 3 * 4 * 16 * 16
+        self.emb = (0.02 * torch.randn(patch, runner.dim, generator=g, device=dev)).to(torch.bfloat16)
+        self.unemb = (0.02 * torch.randn(runner.dim, patch, generator=g, device=dev)).to(torch.bfloat16)
+        self.tokens = 0
+
+    def latent_frames(self):
+        return 6 + 2 * self.n_steps
+
+    @torch.no_grad()
+    def __call__(self, LQ_video, num_frames=None, height=None, width=None, **kwargs):
+        r = self.r
+        crop = LQ_video[0] if LQ_video.dim() == 5 else LQ_video
+        C, F, h, w = crop.shape
+        lf = self.latent_frames()
+        if C != 3 or F < 4 * lf + 1 or h % 16 or w % 16:
+            raise ValueError(f"TiledDiTPipe: crop {tuple(crop.shape)} needs 3 channels, "
+                             f">= {4 * lf + 1} frames and 16-px multiples")
+        hh, ww = h // 16, w // 16
+        # [3, 4*lf, h, w] -> tokens [lf*hh*ww, 3*4*16*16] in (f, h, w) raster order
+        v = crop[:, 1:1 + 4 * lf].to(torch.bfloat16)
+        v = v.reshape(C, lf, 4, hh, 16, ww, 16).permute(1, 3, 5, 0, 2, 4, 6)
+        x = (v.reshape(lf * hh * ww, -1) @ self.emb).unsqueeze(0)
+        per = hh * ww
+        dit = r.dit
+        outs = []
+        f0 = 0
+        caches = None
+        for f in [6] + [2] * self.n_steps:
+            xc = x[:, f0 * per:(f0 + f) * per]
+            fr = dit.chunk_freqs(f, hh, ww, f0, r.device)
+            y, caches = dit.forward_chunk(xc, r.t_mod, fr, (f, hh, ww), caches, topk=r.topk,
+                                          kv_len=r.kv_len)
+            outs.append(y[0])
+            self.tokens += y.shape[1]
+            f0 += f
+        p = torch.cat(outs) @ self.unemb  # [lf*hh*ww, 3*4*16*16]
+        p = p.reshape(lf, hh, ww, C, 4, 16, 16).permute(3, 0, 4, 1, 5, 2, 6)
+        return p.reshape(C, 4 * lf, h, w)

@@ -146,6 +146,84 @@ def _dist_info(group):
     return 1, 0
 
 
+class _TileLoader:
+    """Brings the LQ crops of one rank's tiles onto its GPU ahead of use.
+
+    A crop of a host video is a strided view; copying it as is costs a contiguous host copy
+    plus a synchronous pageable transfer per tile, in series with the tile's compute.  Here
+    a worker thread packs crop k+1 into a pinned staging buffer while the GPU renders tile k,
+    a side stream uploads it, and the render stream waits on an event.  Two staging and two
+    device buffers rotate; the side stream reuses a device buffer only after the render of
+    the tile that used it (an event recorded after its blend).  A video already on the
+    device is cropped there.
+    """
+
+    def __init__(self, lq, tiles, order, device):
+        device = torch.device(device)
+        self.lq, self.tiles, self.order, self.device = lq, tiles, list(order), device
+        self.direct = lq.device == device or device.type != "cuda"
+        if self.direct:
+            return
+        from concurrent.futures import ThreadPoolExecutor
+        C, F = lq.shape[0], lq.shape[1]
+        n = max((tiles[i][2] * tiles[i][3] for i in self.order), default=0) * C * F
+        self.stage = [torch.empty(n, dtype=lq.dtype, pin_memory=True) for _ in range(2)]
+        self.dev = [torch.empty(n, dtype=lq.dtype, device=device) for _ in range(2)]
+        self.copy_stream = torch.cuda.Stream(device)
+        self.up_done = [None, None]    # upload of buffer b finished (host may refill stage b)
+        self.used = [None, None]       # render of the tile in device buffer b finished
+        self.pool = ThreadPoolExecutor(1)
+        self.pending = self.pool.submit(self._pack, 0) if self.order else None
+
+    def _shape(self, k):
+        x, y, w, h = self.tiles[self.order[k]]
+        return self.lq.shape[0], self.lq.shape[1], h, w
+
+    def _pack(self, k):
+        x, y, w, h = self.tiles[self.order[k]]
+        b = k & 1
+        if self.up_done[b] is not None:
+            self.up_done[b].synchronize()  # stage b still feeds an upload in flight
+        shp = self._shape(k)
+        n = shp[0] * shp[1] * shp[2] * shp[3]
+        self.stage[b][:n].view(shp).copy_(self.lq[:, :, y:y + h, x:x + w])
+        return k
+
+    def get(self, k):
+        """Crop of tile order[k] on the device, usable on the current stream."""
+        x, y, w, h = self.tiles[self.order[k]]
+        if self.direct:
+            return self.lq[:, :, y:y + h, x:x + w].to(self.device)
+        self.pending.result()
+        b = k & 1
+        shp = self._shape(k)
+        n = shp[0] * shp[1] * shp[2] * shp[3]
+        with torch.cuda.stream(self.copy_stream):
+            if self.used[b] is not None:
+                self.copy_stream.wait_event(self.used[b])
+            self.dev[b][:n].copy_(self.stage[b][:n], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.copy_stream)
+        self.up_done[b] = ev
+        self.pending = self.pool.submit(self._pack, k + 1) if k + 1 < len(self.order) else None
+        torch.cuda.current_stream(self.device).wait_event(ev)
+        return self.dev[b][:n].view(shp)
+
+    def done(self, k):
+        """The render stream has finished with tile order[k]'s device buffer."""
+        if self.direct:
+            return
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self.used[k & 1] = ev
+
+    def close(self):
+        if not self.direct:
+            if self.pending is not None:
+                self.pending.result()
+            self.pool.shutdown()
+
+
 def render_tiled(pipe, lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
                  tile_threshold=TILE_THRESHOLD, device=None, group=None, **pipe_kwargs):
     """Render lq_video [C,F,H,W] (or [1,C,F,H,W], in [-1, 1]) through `pipe` one tile at a time.
@@ -174,20 +252,25 @@ def render_tiled(pipe, lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
     mine = assign_tiles(len(tiles), world, rank)
     canvas = None
     n_out = torch.zeros(1, dtype=torch.int64, device=device)
-    for i in mine:
-        x, y, w, h = tiles[i]
-        crop = lq[:, :, y:y + h, x:x + w].to(device, non_blocking=True)
-        extra = {"topk_ratio": base_topk * (W * H) / (w * h)} if base_topk is not None else {}
-        frames = pipe(LQ_video=crop.unsqueeze(0) if batched else crop, num_frames=num_frames,
-                      height=h, width=w, **extra, **pipe_kwargs)
-        if canvas is None:
-            canvas = torch.zeros((C, frames.shape[-3], H, W), dtype=torch.float32, device=device)
-            n_out.fill_(frames.shape[-3])
-        elif canvas.shape[1] != frames.shape[-3]:
-            raise RuntimeError(f"tile frame counts diverge: {canvas.shape[1]} vs {frames.shape[-3]}")
-        wgt = tile_weight(x, y, tiles).to(device)
-        canvas[:, :, y:y + h, x:x + w] += frames.to(device=device, dtype=torch.float32) * wgt
-        del frames
+    loader = _TileLoader(lq, tiles, mine, device)
+    try:
+        for k, i in enumerate(mine):
+            x, y, w, h = tiles[i]
+            crop = loader.get(k)
+            extra = {"topk_ratio": base_topk * (W * H) / (w * h)} if base_topk is not None else {}
+            frames = pipe(LQ_video=crop.unsqueeze(0) if batched else crop, num_frames=num_frames,
+                          height=h, width=w, **extra, **pipe_kwargs)
+            if canvas is None:
+                canvas = torch.zeros((C, frames.shape[-3], H, W), dtype=torch.float32, device=device)
+                n_out.fill_(frames.shape[-3])
+            elif canvas.shape[1] != frames.shape[-3]:
+                raise RuntimeError(f"tile frame counts diverge: {canvas.shape[1]} vs {frames.shape[-3]}")
+            wgt = tile_weight(x, y, tiles).to(device)
+            canvas[:, :, y:y + h, x:x + w] += frames.to(device=device, dtype=torch.float32) * wgt
+            loader.done(k)
+            del frames, crop
+    finally:
+        loader.close()
     if world == 1:
         return canvas.to(dtype=lq_video.dtype)
     # every rank needs the output frame count to size its (possibly empty) canvas
