@@ -75,18 +75,46 @@ __device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float a, float b) {
   return (uint16_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
 }
 
-// x / s as the e4m3 conversion will see it, without a full IEEE divide in the common case.
+// GELU(tanh) of x (a bf16 value held in fp32), rounded to bf16: aten's formula
+// 0.5f * x * (1.0f + tanhf(kBeta * (x + kKappa * x^3))) in fp32, rounded once (the
+// rounding fp8_ffn.py:24-30 replicates).
+__device__ __forceinline__ float gelu_tanh_bf16(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
+  const float kKappa = 0.044715f;
+  const float x3 = x * x * x;
+  const float inner = kBeta * __fmaf_rn(kKappa, x3, x);
+  return bf16r(0.5f * x * (1.0f + tanhf(inner)));
+}
+
+// x / s as the e4m3 conversion sees it, without a full IEEE divide in the common case.
 // rs = 1/s correctly rounded.  y = x * rs is within 2 fp32 ulps of the IEEE quotient
 // __fdiv_rn(x, s); their e4m3 roundings (3 mantissa bits kept, round to nearest even) can
 // only differ when y lies within a few ulps of an e4m3 rounding midpoint (fp32 mantissa low
-// 20 bits == 0x80000) or in the e4m3 subnormal range (|y| < 2^-6).  Those inputs take the
-// exact divide, so the resulting code always equals e4m3(__fdiv_rn(x, s)).
-__device__ __forceinline__ float div_for_e4m3(float x, float s, float rs) {
-  const float y = x * rs;
+// 20 bits == 0x80000) or in the e4m3 subnormal range (|y| < 2^-6).  Those inputs must take
+// the exact divide, so the resulting code always equals e4m3(__fdiv_rn(x, s)).
+__device__ __forceinline__ bool e4m3_needs_exact(float y) {
   const uint32_t b = __float_as_uint(y) & 0x7fffffffu;
-  const bool near_mid = ((b & 0xFFFFFu) - 0x80000u + 8u) < 16u;
-  const bool subnormal = b < 0x3C800000u;  // 2^-6
-  return (near_mid || subnormal) ? __fdiv_rn(x, s) : y;
+  return ((b & 0xFFFFFu) - 0x80000u + 8u) < 16u || b < 0x3C800000u /* 2^-6 */;
+}
+
+__device__ __noinline__ uint32_t e4m3x2_exact(float x0, float x1, float s) {
+  return f32x2_to_e4m3x2(__fdiv_rn(x0, s), __fdiv_rn(x1, s));
+}
+
+// 8 fp32 values -> 8 e4m3 codes of clamp(x / s, +-448), rounded to nearest even, packed in
+// a uint2 (the quantisation of fp8_quant.py:16-35).  rs = __frcp_rn(s), hoisted by the
+// caller.  The saturating conversion is the clamp (finite values beyond +-448 go to +-448,
+// NaN stays NaN as clamp-then-cast leaves it).  A pair with a product x * rs that may
+// round differently from the IEEE quotient takes the exact divide (out of line: rare).
+__device__ __forceinline__ uint2 e4m3_codes8(const float* f, float s, float rs) {
+  uint32_t c[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float y0 = f[2 * i] * rs, y1 = f[2 * i + 1] * rs;
+    c[i] = (e4m3_needs_exact(y0) | e4m3_needs_exact(y1)) ? e4m3x2_exact(f[2 * i], f[2 * i + 1], s)
+                                                          : f32x2_to_e4m3x2(y0, y1);
+  }
+  return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -103,6 +131,15 @@ __device__ __forceinline__ float warp_sum(float v) {
 // atomic max on non-negative floats through their bit pattern (monotone for >= 0)
 __device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
   atomicMax(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
+}
+
+// 16-byte read-only load of streamed data (read once: no L1 allocation)
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
 }
 
 // unpack 8 bf16 held in a uint4 into fp32

@@ -4,17 +4,26 @@
 //
 //   out[m, n] = bf16(acc[m, n] * sa[m|0] * sw[n|0] + bias[n]),  acc = sum_k A[m,k] W[n,k]
 //
-// Design (one persistent CTA per SM, 320 threads, warp-specialised):
+// Design (one persistent CTA per SM, 320 or 576 threads, warp-specialised):
 //   warp 0      TMA producer: 128x128-byte A tiles and BNx128-byte W tiles
-//               (128-byte swizzle) into a 4-stage shared-memory ring
+//               (128-byte swizzle) into a 3- or 4-stage shared-memory ring
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma kind::f8f6f4
 //               (M=128, N=BN, K=32 per instruction) into a TMEM accumulator;
 //               tcgen05.commit releases ring stages and publishes finished tiles.
 //               Also allocates / frees the 2*BN TMEM columns.
-//   warps 2-9   epilogue, two warps per TMEM lane quarter: tcgen05.ld 32 columns
-//               at a time (each thread owns one output row, the warp pair splits the
-//               64-column chunks), scales + bias (+ GELU / amax), bf16 into a 128-byte
-//               swizzled staging buffer, TMA bulk store of 32 rows x 64 columns.
+//   warps 2..   epilogue, G warps per TMEM lane quarter (G = 2 for the plain
+//               epilogue, 4 for GELU + amax, whose per-warp latency is the long pole):
+//               tcgen05.ld 32 columns at a time (each thread owns one output row, the G
+//               warps take the 64-column chunks round-robin), scales + bias (+ GELU /
+//               amax), bf16 into a 128-byte swizzled staging buffer, TMA bulk store of
+//               32 rows x 64 columns.  The GELU variant runs a 3-stage ring to make room
+//               for its 16 staging buffers and its GELU table.
+// GELU epilogue: the GELU input is the bf16-rounded GEMM output, so GELU is a function of
+// 16 bits.  Each CTA tabulates it (exact formula, gelu_tanh_bf16) for |x| in [2^-9, 16)
+// into 6.5 KB of shared memory while its first tile's main loop runs; the epilogue then
+// costs one shared-memory load per element instead of a tanh.  Outside the table the
+// results are 0.5 x (|x| < 2^-9: 1 + tanh u rounds to 1 within half a bf16 ulp), x
+// (x >= 16) and x * 0 (x <= -16: tanh u is -1); the tests check every bf16 input.
 // The accumulator is double-buffered in TMEM so the epilogue of tile t overlaps
 // the main loop of tile t+1.  Both operands are K-major ("TN"), exactly the
 // nn.Linear weight layout, so no transpose is ever materialised.
@@ -25,9 +34,14 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes == fp8 elements per K block
-constexpr int STAGES = 4;
-constexpr int EPI_WARPS = 8;
-constexpr int THREADS = 64 + 32 * EPI_WARPS;
+
+// per-epilogue configuration: epilogue warps (a multiple of 4) and ring depth
+template <int EPI>
+struct Cfg {
+  static constexpr int kEpiWarps = EPI == FVB_EPI_GELU_AMAX ? 16 : 8;
+  static constexpr int kStages = EPI == FVB_EPI_GELU_AMAX ? 3 : 4;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+};
 
 struct Args {
   int M, N, K;
@@ -41,32 +55,51 @@ struct Args {
 };
 
 constexpr int kStageBytes = 32 * 128;  // one epilogue warp's 32 rows x 64 bf16 columns
-constexpr int kOutBytes = EPI_WARPS * kStageBytes;  // one staging buffer per warp
 
-template <int BN>
+// GELU table: bf16 bit patterns with |x| in [2^-9, 16) = [0x3B00, 0x4180), both signs
+constexpr uint32_t kGeluLo = 0x3B00u;
+constexpr uint32_t kGeluRange = 0x4180u - kGeluLo;  // 1664 entries per sign
+template <int EPI>
+struct Lut {
+  static constexpr int kBytes = EPI == FVB_EPI_GELU_AMAX ? (int)(2 * kGeluRange * 2) : 0;
+};
+
+template <int BN, int EPI>
 constexpr size_t smem_bytes() {
-  return (size_t)STAGES * (BM + BN) * BK + kOutBytes + 1024 /*align slack*/ + 256 /*barriers*/;
+  return (size_t)Cfg<EPI>::kStages * (BM + BN) * BK + (size_t)Cfg<EPI>::kEpiWarps * kStageBytes +
+         Lut<EPI>::kBytes + 1024 /*align slack*/ + 256 /*barriers*/;
 }
 
-__device__ __forceinline__ float gelu_tanh_bf16_epi(float x) {
-  const float kBeta = 0.7978845608028654f;
-  const float kKappa = 0.044715f;
-  float x3 = x * x * x;
-  float inner = kBeta * __fmaf_rn(kKappa, x3, x);
-  return bf16r(0.5f * x * (1.0f + tanhf(inner)));
+__device__ __forceinline__ uint32_t bf16_bits_rn(float x) {
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+// bf16 bits of GELU(bf16(o)) through the shared-memory table (see the header comment)
+__device__ __forceinline__ uint32_t gelu_bits(float o, const uint16_t* lut) {
+  const uint32_t h = bf16_bits_rn(o);
+  const uint32_t a = h & 0x7FFFu;
+  const uint32_t k = a - kGeluLo;
+  if (k < kGeluRange) return lut[(h >> 15) * kGeluRange + k];
+  const float x = __uint_as_float(h << 16);
+  return bf16_bits_rn(a < kGeluLo ? 0.5f * x : ((h & 0x8000u) ? x * 0.0f : x));
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmOut, const Args args) {
+  constexpr int STAGES = Cfg<EPI>::kStages;
+  constexpr int EPI_WARPS = Cfg<EPI>::kEpiWarps;
+  constexpr int G = EPI_WARPS / 4;  // epilogue warps per TMEM lane quarter
+  constexpr int kOutBytes = EPI_WARPS * kStageBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
   uint8_t* sA = base;
   uint8_t* sB = sA + STAGES * BM * BK;
   uint8_t* sOut = sB + STAGES * BN * BK;  // epilogue staging, 1024-aligned
-  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + kOutBytes);
+  uint16_t* lut = reinterpret_cast<uint16_t*>(sOut + kOutBytes);  // GELU table (GELU only)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + kOutBytes + Lut<EPI>::kBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -165,10 +198,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // 8 warps: two per TMEM lane quarter (warp % 4); the pair splits each tile's 64-column
-    // chunks between them (even / odd chunks), so each thread finishes half a row per tile.
+    // G warps per TMEM lane quarter (warp % 4); they take each tile's 64-column chunks
+    // round-robin, so each thread finishes 1/G of a row per tile.
     const int q = warp & 3;               // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;     // 0: warps 2-5, 1: warps 6-9
+    const int half = (warp - 2) >> 2;     // 0..G-1: this warp's first chunk
+    if (EPI == FVB_EPI_GELU_AMAX) {
+      // tabulate GELU while the first tile's main loop runs; epilogue warps only
+      for (uint32_t i = threadIdx.x - 64; i < 2 * kGeluRange; i += EPI_WARPS * 32) {
+        const uint32_t neg = i >= kGeluRange;
+        const uint32_t h = (neg << 15) | (kGeluLo + i - neg * kGeluRange);
+        lut[i] = (uint16_t)bf16_bits_rn(gelu_tanh_bf16(__uint_as_float(h << 16)));
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32) : "memory");
+    }
     uint8_t* stg = sOut + (size_t)(warp - 2) * kStageBytes;  // this warp's staging, 32 x 128 B
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
@@ -183,9 +225,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool row_ok = row < args.M;
       const float sa = args.a_row ? (row_ok ? __ldg(args.sa + row) : 0.f) : __ldg(args.sa);
       const float sw0 = args.w_row ? 0.f : __ldg(args.sw);
-      float tmax = 0.f;
+      uint32_t tmax = 0;  // row amax of |GELU| as bf16 magnitude bits (GELU only)
 #pragma unroll 1
-      for (int c = half; c < BN / 64; c += 2) {
+      for (int c = half; c < BN / 64; c += G) {
         const int col0 = n0 + c * 64;
         // the previous TMA store from this staging buffer must have finished reading it
         if (lane == 0) tma_store_wait_read<0>();
@@ -217,21 +259,29 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
               for (int i = 0; i < 8; ++i) bv[i] = 0.f;
             }
+            uint4 packed;
+            if (EPI == FVB_EPI_GELU_AMAX) {
+              uint32_t hb[8];
+              const bool counted = row_ok && cg < args.N;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float o = __fmaf_rn(__uint_as_float(r[g4 * 8 + i]), sa * swv[i], bv[i]);
-              if (EPI == FVB_EPI_GELU_AMAX) {
-                o = gelu_tanh_bf16_epi(bf16r(o));
-                if (row_ok && cg < args.N) tmax = fmaxf(tmax, fabsf(o));
+              for (int i = 0; i < 8; ++i) {
+                hb[i] = gelu_bits(__fmaf_rn(__uint_as_float(r[g4 * 8 + i]), sa * swv[i], bv[i]),
+                                  lut);
+                if (counted) tmax = max(tmax, hb[i] & 0x7FFFu);
               }
-              v[i] = o;
+              packed = make_uint4(__byte_perm(hb[0], hb[1], 0x5410), __byte_perm(hb[2], hb[3], 0x5410),
+                                  __byte_perm(hb[4], hb[5], 0x5410), __byte_perm(hb[6], hb[7], 0x5410));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                v[i] = __fmaf_rn(__uint_as_float(r[g4 * 8 + i]), sa * swv[i], bv[i]);
+              packed = f32_to_bf16x8(v);
             }
             // 128-byte swizzle: 16-byte chunk g of row `lane` lands at chunk g ^ (lane & 7)
-            *reinterpret_cast<uint4*>(stg + lane * 128 + ((g ^ (lane & 7)) << 4)) =
-                f32_to_bf16x8(v);
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((g ^ (lane & 7)) << 4)) = packed;
           }
         }
-        if (c + 2 >= BN / 64) {  // this warp's last TMEM read of the tile
+        if (c + G >= BN / 64) {  // this warp's last TMEM read of the tile
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -243,12 +293,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_store_commit();
         }
       }
+      if (half >= BN / 64) {  // a warp with no chunk in this tile (G > BN / 64)
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+      }
       if (EPI == FVB_EPI_GELU_AMAX) {
+        // bf16 magnitude bits order like the values they encode (NaN above +inf)
         if (args.a_row) {
-          if (row_ok) atomic_max_nonneg(args.amax_out + row, tmax);
+          if (row_ok) atomic_max_nonneg(args.amax_out + row, __uint_as_float(tmax << 16));
         } else {
-          tmax = warp_max(tmax);
-          if (lane == 0) atomic_max_nonneg(args.amax_out, tmax);
+          const uint32_t m = __reduce_max_sync(0xffffffffu, tmax);
+          if (lane == 0) atomic_max_nonneg(args.amax_out, __uint_as_float(m << 16));
         }
       }
     }
@@ -276,7 +332,8 @@ static int launch(const Args& a, const void* A, const void* W, cudaStream_t st) 
                     (uint64_t)a.ldo * 2, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   auto kern = fp8_gemm_kernel<BN, EPI>;
-  constexpr size_t smem = smem_bytes<BN>();
+  constexpr size_t smem = smem_bytes<BN, EPI>();
+  static_assert(smem <= 227 * 1024, "fp8 gemm: shared memory");
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -288,7 +345,7 @@ static int launch(const Args& a, const void* A, const void* W, cudaStream_t st) 
   const int tiles = ((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
   int grid = sm_count();
   if (tiles < grid) grid = tiles;
-  kern<<<grid, THREADS, smem, st>>>(tmA, tmB, tmO, a);
+  kern<<<grid, Cfg<EPI>::kThreads, smem, st>>>(tmA, tmB, tmO, a);
   return check_launch("fvb_fp8_gemm");
 }
 

@@ -25,19 +25,11 @@ __device__ __forceinline__ float quant_scale_from_amax_n(float amax) {
 }
 
 // Per-token e4m3 codes of 8 bf16 values held in a uint4 (the bf16 output of a row kernel):
-// q = e4m3_rn_satfinite(clamp(y / qs)), with the divide of div_for_e4m3.
+// q = e4m3_rn(clamp(y / qs, +-448)).
 __device__ __forceinline__ uint2 fp8_codes8(const uint4& y, float qs, float rqs) {
   float f[8];
   bf16x8_to_f32(y, f);
-  uint32_t w[2];
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    float a[4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) a[t] = fminf(fmaxf(div_for_e4m3(f[4 * hh + t], qs, rqs), -448.f), 448.f);
-    w[hh] = (uint32_t)f32x2_to_e4m3x2(a[0], a[1]) | ((uint32_t)f32x2_to_e4m3x2(a[2], a[3]) << 16);
-  }
-  return make_uint2(w[0], w[1]);
+  return e4m3_codes8(f, qs, rqs);
 }
 
 // Row mean and (x - mean) * rden with rden = 1/sqrt(var + eps), two-pass in registers.

@@ -19,36 +19,12 @@ namespace fvb {
 
 constexpr float kFp8Max = 448.0f;
 
-// GELU with the tanh approximation, evaluated like PyTorch's CUDA kernel for
-// F.gelu(approximate="tanh") on a bf16 tensor: fp32 math, result rounded to
-// bf16 (fp8_ffn.py:24-30 mirrors the same bf16 output rounding).
-__device__ __forceinline__ float gelu_tanh_bf16(float x) {
-  const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
-  const float kKappa = 0.044715f;
-  float x3 = x * x * x;
-  float inner = kBeta * __fmaf_rn(kKappa, x3, x);
-  float y = 0.5f * x * (1.0f + tanhf(inner));
-  return bf16r(y);
-}
-
 __device__ __forceinline__ float quant_scale_from_amax(float amax) {
   return __fdiv_rn(fmaxf(amax, 1e-12f), kFp8Max);
 }
 
-__device__ __forceinline__ float clamp448(float v) { return fminf(fmaxf(v, -kFp8Max), kFp8Max); }
-
-// 8 values -> 8 e4m3 codes packed in a uint2; rs = __frcp_rn(s), hoisted by the caller
 __device__ __forceinline__ uint2 quant8(const float* f, float s, float rs) {
-  uint32_t w[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    uint16_t lo = f32x2_to_e4m3x2(clamp448(div_for_e4m3(f[4 * h + 0], s, rs)),
-                                  clamp448(div_for_e4m3(f[4 * h + 1], s, rs)));
-    uint16_t hi = f32x2_to_e4m3x2(clamp448(div_for_e4m3(f[4 * h + 2], s, rs)),
-                                  clamp448(div_for_e4m3(f[4 * h + 3], s, rs)));
-    w[h] = (uint32_t)lo | ((uint32_t)hi << 16);
-  }
-  return make_uint2(w[0], w[1]);
+  return e4m3_codes8(f, s, rs);
 }
 
 template <bool GELU>
@@ -114,7 +90,7 @@ __global__ void __launch_bounds__(256) quant_tensor_kernel(
     for (int64_t i = nvec * 8 + threadIdx.x; i < n; i += blockDim.x) {
       float f = __bfloat162float(xs[i]);
       if (GELU) f = gelu_tanh_bf16(f);
-      qs[i] = f32_to_e4m3(clamp448(__fdiv_rn(f, s)));
+      qs[i] = f32_to_e4m3(__fdiv_rn(f, s));  // saturating == clamp
     }
   }
 }
@@ -200,36 +176,51 @@ __global__ void __launch_bounds__(256) quant_row_long_kernel(const __nv_bfloat16
   if (lane == 0) scale_out[row] = __fdiv_rn(m, kFp8Max);
 }
 
-// Rows are dealt to blocks; the scale and its reciprocal are computed once per row and
-// each thread keeps four 16-byte loads in flight.  (A flat grid-stride loop over the
-// whole matrix spent more time in its 64-bit row = v / (K/8) divides than in memory.)
-__global__ void __launch_bounds__(256) quant_with_amax_kernel(
+// Quantisation with a precomputed amax (the second half of fused_gelu_quant_fp8,
+// fp8_ffn.py:57-72, once the GEMM epilogue has reduced the row amax).  One warp per row:
+// the scale and its reciprocal are computed once per row, and each lane keeps six
+// 16-byte loads in flight; 4 blocks of 8 warps are resident per SM.  (A flat grid-stride
+// loop over the whole matrix spent more time in its 64-bit row = v / (K/8) divides than
+// in memory; a block per row left most threads idle in the row's tail.)
+constexpr int kQaUnroll = 6;
+__global__ void __launch_bounds__(256, 4) quant_with_amax_kernel(
     const uint4* __restrict__ g, int64_t M, int64_t K, const float* __restrict__ amax, int per_row,
     uint2* __restrict__ q, float* __restrict__ scale_out) {
-  const int kv = (int)(K >> 3);  // vectors per row (K < 2^34 enforced by the host)
-  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+  const int kv = (int)(K >> 3);  // vectors per row (K / 8 < 2^31 enforced by the host)
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * 8;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < M; row += nwarps) {
     const float a = __ldg(amax + (per_row ? row : 0));
     const float s = quant_scale_from_amax(a);
     const float rs = __frcp_rn(s);
-    if (threadIdx.x == 0 && (per_row || row == 0)) scale_out[per_row ? row : 0] = __fdiv_rn(a, kFp8Max);
+    if (lane == 0 && (per_row || row == 0)) scale_out[per_row ? row : 0] = __fdiv_rn(a, kFp8Max);
     const uint4* gr = g + row * kv;
     uint2* qr = q + row * kv;
-    int v = threadIdx.x;
-    for (; v + 3 * 256 < kv; v += 4 * 256) {
-      uint4 u[4];
+    int v = lane;
+    for (; v + (kQaUnroll - 1) * 32 < kv; v += kQaUnroll * 32) {
+      uint4 u[kQaUnroll];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) u[t] = __ldg(gr + v + t * 256);
+      for (int t = 0; t < kQaUnroll; ++t) u[t] = ld_stream(gr + v + t * 32);
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
+      for (int t = 0; t < kQaUnroll; ++t) {
         float f[8];
         bf16x8_to_f32(u[t], f);
-        qr[v + t * 256] = quant8(f, s, rs);
+        qr[v + t * 32] = quant8(f, s, rs);
       }
     }
-    for (; v < kv; v += 256) {
-      float f[8];
-      bf16x8_to_f32(__ldg(gr + v), f);
-      qr[v] = quant8(f, s, rs);
+    if (v < kv) {  // the row's tail: fewer than kQaUnroll vectors per lane
+      uint4 u[kQaUnroll];
+#pragma unroll
+      for (int t = 0; t < kQaUnroll; ++t)
+        if (v + t * 32 < kv) u[t] = ld_stream(gr + v + t * 32);
+#pragma unroll
+      for (int t = 0; t < kQaUnroll; ++t) {
+        if (v + t * 32 < kv) {
+          float f[8];
+          bf16x8_to_f32(u[t], f);
+          qr[v + t * 32] = quant8(f, s, rs);
+        }
+      }
     }
   }
 }
@@ -325,8 +316,8 @@ int fvb_quant_fp8_with_amax(const void* g, int64_t M, int64_t K, const float* am
   FVB_REQUIRE(aligned16(g) && (reinterpret_cast<uintptr_t>(q) & 7u) == 0,
               "fvb_quant_fp8_with_amax: misaligned pointer");
   FVB_REQUIRE(K / 8 <= 0x7fffffff, "fvb_quant_fp8_with_amax: row too long");
-  const int64_t rows_grid = M < (int64_t)sm_count() * 8 ? M : (int64_t)sm_count() * 8;
-  quant_with_amax_kernel<<<(unsigned)rows_grid, 256, 0, (cudaStream_t)stream>>>(
+  const int64_t blocks = (M + 7) / 8, cap = (int64_t)sm_count() * 8;
+  quant_with_amax_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, (cudaStream_t)stream>>>(
       (const uint4*)g, M, K, amax, mode == FVB_SCALE_ROW, (uint2*)q, scale_out);
   return check_launch("fvb_quant_fp8_with_amax");
 }

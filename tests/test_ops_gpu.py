@@ -233,6 +233,29 @@ def test_fp8_gemm_gelu_epilogue_amax():
     assert torch.equal(amax, ge.float().abs().amax(dim=1))
 
 
+def test_gelu_epilogue_every_bf16_input():
+    """Every bf16 value (finite and infinite) through the GELU epilogue: A is zero, so the
+    bias column carries x, and each output must equal eager GELU of the plain GEMM output
+    bit for bit (the table's range and the rules outside it are checked exhaustively)."""
+    from flashvsr_sm89_ops_b200 import _lib
+    from flashvsr_sm89_ops_b200.fp8_linear import fp8_mm
+    x = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    x = torch.where(torch.isnan(x), torch.zeros_like(x), x).to(DEV)
+    M, K, N = 32, 16, x.numel()
+    qa = torch.zeros(M, K, dtype=torch.float8_e4m3fn, device=DEV)
+    qw = torch.zeros(N, K, dtype=torch.float8_e4m3fn, device=DEV)
+    one = torch.ones(1, device=DEV)
+    amax = torch.zeros(1, device=DEV)
+    h = fp8_mm(qa, one, qw, one, x, epilogue=_lib.FVB_EPI_GELU_AMAX, amax_out=amax)
+    plain = fp8_mm(qa, one, qw, one, x)
+    ge = F.gelu(plain, approximate="tanh")
+    nan = torch.isnan(ge)
+    assert torch.equal(torch.isnan(h), nan)
+    hv, gv = h.view(torch.int16)[~nan], ge.view(torch.int16)[~nan]
+    bad = (hv != gv).sum().item()
+    assert bad == 0, f"{bad} of {hv.numel()} GELU outputs differ from eager"
+
+
 @pytest.mark.parametrize("mode", ["tensor", "token"])
 def test_fp8_ffn(mode):
     from flashvsr_sm89_ops_b200.fp8_ffn import FP8FFN
