@@ -58,6 +58,8 @@ _SIGS = {
     "fvb_draft_mask_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "fvb_draft_block_mask": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "fvb_causal_topk_mask": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp]),
+    "fvb_block_mean_pool": (_int, [_vp, _i64, _i64, _vp, _vp]),
+    "fvb_causal_topk_pooled": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp]),
 }
 
 

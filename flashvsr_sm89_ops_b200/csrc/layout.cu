@@ -244,50 +244,142 @@ __global__ void __launch_bounds__(1024) draft_topk_kernel(const float* __restric
 }
 
 // ---------------------------------------------------------------------------
-// causal top-k rule (benchmark measurement input).  grid (NQ, H), block 256,
-// dynamic smem 2*NK floats.  Scores use fp32 pooled means.
+// causal top-k rule (benchmark measurement input) from pooled fp32 means.
+// grid (H, ceil(NQ / kTopkQ)), block 256: one CTA per head and group of kTopkQ query
+// blocks, so a head's pooled keys cross L2 once per group, not once per query block.
+//   1. the group's query vectors go to shared memory;
+//   2. key rows stream through shared memory 128 at a time (16-byte asynchronous
+//      copies, all in flight at once; a row pitch of d + 4 floats keeps the
+//      per-thread 16-byte reads conflict-free);
+//      thread (r, half) scores key row r against half of the group's queries;
+//   3. warp w selects for query w: scores become order-preserving integer keys, the
+//      nsel-th largest key is found bit by bit (32 warp-wide counts), and keys equal to
+//      it are taken in index order, so ties go to the lower key index;
+//   4. the warp writes the query's keep row: own time row, selected past blocks, never
+//      a future row.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) causal_topk_kernel(const float* __restrict__ aq,
-                                                           const float* __restrict__ ak,
-                                                           int64_t NQ, int64_t NK, int H, int d,
-                                                           int64_t per_row, float ratio,
-                                                           uint8_t* __restrict__ keep) {
-  extern __shared__ float sc[];
-  const int64_t qi = blockIdx.x;
-  const int h = blockIdx.y;
+constexpr int kTopkThreads = 256;
+constexpr int kTopkQ = 8;    // query blocks per CTA (one selecting warp each)
+constexpr int kTopkKC = 128;  // key rows per shared-memory chunk
+
+__device__ __forceinline__ uint32_t ordered_key(float s) {
+  const uint32_t u = __float_as_uint(s + 0.0f);  // -0 -> +0: equal scores, equal keys
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kTopkThreads) causal_topk_kernel(
+    const float* __restrict__ aq, const float* __restrict__ ak, int NQ, int NK, int H, int d,
+    int per_row, float ratio, uint8_t* __restrict__ keep) {
+  extern __shared__ float4 dyn4[];
+  const int h = blockIdx.x;
+  const int q0 = blockIdx.y * kTopkQ;
+  const int nq = min(kTopkQ, NQ - q0);
+  const int pitch4 = (d >> 2) + 1;  // key row pitch in float4
+  const int d4 = d >> 2;
+  float4* qs4 = dyn4;                             // [kTopkQ][d4]
+  float4* ks4 = qs4 + kTopkQ * d4;                // [kTopkKC][pitch4]
+  uint32_t* key = reinterpret_cast<uint32_t*>(ks4 + kTopkKC * pitch4);  // [kTopkQ][NK]
   const int64_t C = (int64_t)H * d;
-  const int64_t cache_rows = (NK - NQ) / per_row;
-  const int64_t qrow = cache_rows + qi / per_row;  // global time row of the query block
-  const int64_t npast = qrow * per_row;            // key blocks in earlier rows
-  const int64_t nsel = (int64_t)floorf(ratio * (float)npast);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const float* qv = aq + qi * C + (int64_t)h * d;
-  for (int64_t kj = wid; kj < npast; kj += nw) {
-    const float* kv = ak + kj * C + (int64_t)h * d;
-    float acc = 0.f;
-    for (int e = lane; e < d; e += 32) acc = __fmaf_rn(qv[e], kv[e], acc);
-    acc = warp_sum(acc);
-    if (lane == 0) sc[kj] = acc;
+  const int cache_rows = (NK - NQ) / per_row;
+  // past key blocks of the group's last query (the most any of its queries needs)
+  const int np_max = (cache_rows + (q0 + nq - 1) / per_row) * per_row;
+
+  for (int i = threadIdx.x; i < nq * d4; i += kTopkThreads) {
+    const int qq = i / d4, e = i - qq * d4;
+    cp_async16(qs4 + i, reinterpret_cast<const float4*>(aq + (int64_t)(q0 + qq) * C + (int64_t)h * d) + e);
   }
-  __syncthreads();
-  uint8_t* kp = keep + ((int64_t)h * NQ + qi) * NK;
-  for (int64_t kj = threadIdx.x; kj < NK; kj += blockDim.x) {
-    const int64_t krow = kj / per_row;
-    uint8_t on = 0;
-    if (krow == qrow) {
-      on = 1;
-    } else if (krow < qrow) {
-      // rank among past blocks: larger score first, ties by lower index
-      const float s = sc[kj];
-      int64_t rank = 0;
-      for (int64_t o = 0; o < npast; ++o) {
-        const float so = sc[o];
-        rank += (so > s) || (so == s && o < kj);
-      }
-      on = rank < nsel;
+  const int r = threadIdx.x & (kTopkKC - 1);
+  const int half = threadIdx.x / kTopkKC;  // queries half, half + 2, ...
+  for (int k0 = 0; k0 < np_max; k0 += kTopkKC) {
+    const int kn = min(kTopkKC, np_max - k0);
+    __syncthreads();  // previous chunk fully read
+    for (int i = threadIdx.x; i < kn * d4; i += kTopkThreads) {
+      const int rr = i / d4, e = i - rr * d4;
+      cp_async16(ks4 + rr * pitch4 + e,
+                 reinterpret_cast<const float4*>(ak + (int64_t)(k0 + rr) * C + (int64_t)h * d) + e);
     }
-    kp[kj] = on;
+    cp_async_wait_all();  // this thread's copies (and, first time, the query vectors)
+    __syncthreads();
+    if (r < kn) {
+      float acc[kTopkQ / 2];
+#pragma unroll
+      for (int j = 0; j < kTopkQ / 2; ++j) acc[j] = 0.f;
+      const float4* kr = ks4 + r * pitch4;
+      for (int e = 0; e < d4; ++e) {
+        const float4 kk = kr[e];
+#pragma unroll
+        for (int j = 0; j < kTopkQ / 2; ++j) {
+          const float4 qv = qs4[(half + 2 * j) * d4 + e];  // same address across the warp
+          acc[j] = __fmaf_rn(qv.x, kk.x, acc[j]);
+          acc[j] = __fmaf_rn(qv.y, kk.y, acc[j]);
+          acc[j] = __fmaf_rn(qv.z, kk.z, acc[j]);
+          acc[j] = __fmaf_rn(qv.w, kk.w, acc[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kTopkQ / 2; ++j) {
+        const int qq = half + 2 * j;
+        if (qq < nq) key[qq * NK + k0 + r] = ordered_key(acc[j]);
+      }
+    }
   }
+  cp_async_wait_all();  // np_max == 0: the query copies were never waited for
+  __syncthreads();
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (w >= nq) return;
+  const int qi = q0 + w;
+  const int qrow = cache_rows + qi / per_row;
+  const int npast = qrow * per_row;
+  const int nsel = (int)floorf(ratio * (float)npast);
+  const uint32_t* kq = key + w * NK;
+  // largest T with #{key >= T} >= nsel, i.e. the nsel-th largest key
+  uint32_t T = 0;
+  if (nsel > 0) {
+    for (int b = 31; b >= 0; --b) {
+      const uint32_t cand = T | (1u << b);
+      int c = 0;
+      for (int i = lane; i < npast; i += 32) c += kq[i] >= cand;
+      if ((int)__reduce_add_sync(0xffffffffu, (unsigned)c) >= nsel) T = cand;
+    }
+  }
+  int gt = 0;
+  for (int i = lane; i < npast; i += 32) gt += kq[i] > T;
+  const int need = nsel - (int)__reduce_add_sync(0xffffffffu, (unsigned)gt);  // ties to keep
+  uint8_t* kp = keep + ((int64_t)h * NQ + qi) * NK;
+  const unsigned lt = (1u << lane) - 1u;
+  int eq_before = 0;
+  for (int k0 = 0; k0 < NK; k0 += 32) {
+    const int kj = k0 + lane;
+    const bool past = kj < npast;
+    const uint32_t kv = past ? kq[kj] : 0u;
+    const bool eq = past && nsel > 0 && kv == T;
+    const unsigned bal = __ballot_sync(0xffffffffu, eq);
+    const bool tie_kept = eq && (eq_before + __popc(bal & lt)) < need;
+    eq_before += __popc(bal);
+    if (kj < NK) {
+      const int krow = kj / per_row;
+      kp[kj] = (krow == qrow) || (past && nsel > 0 && (kv > T || tie_kept)) ? 1 : 0;
+    }
+  }
+}
+
+// query vectors + one key chunk (padded rows) + the group's integer score keys
+static size_t causal_topk_smem(int64_t NK, int64_t d) {
+  return ((size_t)kTopkQ * (d / 4) + (size_t)kTopkKC * (d / 4 + 1)) * 16 + (size_t)kTopkQ * NK * 4;
+}
+
+static int launch_causal_topk(const float* aq, const float* ak, int64_t H, int64_t NQ, int64_t NK,
+                              int64_t d, int64_t per_row, float ratio, uint8_t* keep,
+                              cudaStream_t st) {
+  const size_t smem = causal_topk_smem(NK, d);
+  if (smem > 48 * 1024)
+    FVB_CUDA_TRY(cudaFuncSetAttribute(causal_topk_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "causal_topk smem");
+  causal_topk_kernel<<<dim3((unsigned)H, (unsigned)((NQ + kTopkQ - 1) / kTopkQ)), kTopkThreads,
+                       smem, st>>>(aq, ak, (int)NQ, (int)NK, (int)H, (int)d, (int)per_row, ratio,
+                                   keep);
+  return check_launch("fvb_causal_topk_mask");
 }
 
 static inline unsigned warp_rows_grid(int64_t rows) { return (unsigned)((rows + 7) / 8); }
@@ -375,13 +467,14 @@ int fvb_causal_topk_mask(const void* q_w, const void* k_w, int64_t H, int64_t NQ
                          fvb_stream_t stream) {
   using namespace fvb;
   cudaStream_t st = (cudaStream_t)stream;
-  FVB_REQUIRE(H > 0 && NQ > 0 && NK >= NQ && d > 0 && (H * d) % 8 == 0,
+  FVB_REQUIRE(H > 0 && NQ > 0 && NK >= NQ && d > 0 && d % 4 == 0 && (H * d) % 8 == 0,
               "fvb_causal_topk_mask: shape");
   FVB_REQUIRE(per_row > 0 && NQ % per_row == 0 && NK % per_row == 0,
               "fvb_causal_topk_mask: blocks per time row must divide NQ and NK");
   FVB_REQUIRE(q_w && k_w && keep && workspace, "fvb_causal_topk_mask: NULL pointer");
   FVB_REQUIRE(aligned16(q_w) && aligned16(k_w), "fvb_causal_topk_mask: alignment");
-  FVB_REQUIRE(NK * 4 <= 200 * 1024, "fvb_causal_topk_mask: NK too large");
+  FVB_REQUIRE(NK < (1ll << 31) / H && causal_topk_smem(NK, d) <= 200 * 1024,
+              "fvb_causal_topk_mask: NK or d too large");
   const int64_t C = H * d;
   float* aq = static_cast<float*>(workspace);
   float* ak = aq + NQ * C;
@@ -389,14 +482,31 @@ int fvb_causal_topk_mask(const void* q_w, const void* k_w, int64_t H, int64_t NQ
   pool_kernel<<<dim3((unsigned)NK, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 0, ak);
   int rc = check_launch("fvb_causal_topk_mask pool");
   if (rc) return rc;
-  const size_t smem = (size_t)NK * 4;
-  if (smem > 48 * 1024)
-    FVB_CUDA_TRY(cudaFuncSetAttribute(causal_topk_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                 "causal_topk smem");
-  causal_topk_kernel<<<dim3((unsigned)NQ, (unsigned)H), 256, smem, st>>>(
-      aq, ak, NQ, NK, (int)H, (int)d, per_row, ratio, keep);
-  return check_launch("fvb_causal_topk_mask");
+  return launch_causal_topk(aq, ak, H, NQ, NK, d, per_row, ratio, keep, st);
+}
+
+int fvb_block_mean_pool(const void* x, int64_t nblk, int64_t C, float* out, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(nblk >= 0 && C > 0 && C % 8 == 0, "fvb_block_mean_pool: shape");
+  if (nblk == 0) return FVB_OK;
+  FVB_REQUIRE(x && out && aligned16(x), "fvb_block_mean_pool: pointers");
+  pool_kernel<<<dim3((unsigned)nblk, (unsigned)((C + 511) / 512)), 256, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)x, nblk, C, 0, out);
+  return check_launch("fvb_block_mean_pool");
+}
+
+int fvb_causal_topk_pooled(const float* aq, const float* ak, int64_t H, int64_t NQ, int64_t NK,
+                           int64_t d, int64_t per_row, float ratio, uint8_t* keep,
+                           fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(H > 0 && NQ > 0 && NK >= NQ && d > 0 && d % 4 == 0,
+              "fvb_causal_topk_pooled: shape");
+  FVB_REQUIRE(per_row > 0 && NQ % per_row == 0 && NK % per_row == 0,
+              "fvb_causal_topk_pooled: blocks per time row must divide NQ and NK");
+  FVB_REQUIRE(aq && ak && keep && aligned16(aq) && aligned16(ak), "fvb_causal_topk_pooled: pointers");
+  FVB_REQUIRE(NK < (1ll << 31) / H && causal_topk_smem(NK, d) <= 200 * 1024,
+              "fvb_causal_topk_pooled: NK or d too large");
+  return launch_causal_topk(aq, ak, H, NQ, NK, d, per_row, ratio, keep, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -24,6 +24,7 @@ Extra flags of this pack: FS89_FP8_SCALE=token|tensor (activation granularity;
 from __future__ import annotations
 
 import os
+import weakref
 
 import torch
 
@@ -114,17 +115,85 @@ def _local_mask(self, dit, h, w, local_range, device):
     return self.local_attn_mask
 
 
-def _keep_mask(self, dit, q_w, k_w, nh, seqlen, h, w, topk, local_range):
+class _KVArena:
+    """Key (or value) window rows of one self-attention stream, in a buffer with spare
+    time rows, so a streaming step writes its new row right after the cache it was given
+    and attends to one contiguous [cache | new] view instead of concatenating them.
+
+    ``views`` keeps a weak reference to every cache tensor handed out, with its window
+    range; a range is written only while no live handed-out cache covers it, so a cache
+    a caller still holds never changes underneath it.
+    """
+
+    SPARE_ROWS = 4  # time rows of headroom: one copy of the cache per 4 streaming steps
+
+    def __init__(self, nblk, D, device):
+        self.buf = torch.empty((nblk * 128, D), dtype=torch.bfloat16, device=device)
+        self.cap = nblk
+        self.views = []
+
+    def covered(self, a, b):
+        """Whether a live handed-out cache covers any window of [a, b)."""
+        self.views = [v for v in self.views if v[0]() is not None]
+        return any(x < b and a < y for _, x, y in self.views)
+
+    def rows(self, a, b):
+        return self.buf[a * 128:b * 128]
+
+    def hand_out(self, a, b):
+        t = self.rows(a, b).view(b - a, 128, -1)
+        t._fvb_arena = (self, a, b)
+        self.views.append((weakref.ref(t), a, b))
+        return t
+
+
+def _arena_slot(pre, nnew, row_blocks, D, device):
+    """(arena, a, b) with the cache `pre` in windows [a, b) of an arena whose windows
+    [b, b + nnew) are free for the new time row: `pre`'s own arena when it came from
+    one and has room, else a new arena holding a copy of `pre`."""
+    st = getattr(pre, "_fvb_arena", None) if pre is not None else None
+    if st is not None:
+        ar, a, b = st
+        if ar.buf.shape[1] == D and ar.buf.device == device and b + nnew <= ar.cap \
+                and not ar.covered(b, b + nnew):
+            return ar, a, b
+    npre = 0 if pre is None else pre.numel() // (128 * D)
+    ar = _KVArena(npre + nnew + row_blocks * _KVArena.SPARE_ROWS, D, device)
+    if npre:
+        ar.rows(0, npre).copy_(pre.reshape(-1, D))
+    return ar, 0, npre
+
+
+def _cached_kpool(cache_k, D):
+    """Pooled key means stored with a KV-cache tensor this module returned, if the tensor
+    is unchanged since (same in-place version counter) and the shapes agree."""
+    st = getattr(cache_k, "_fvb_kpool", None) if cache_k is not None else None
+    if st is None or st[1] != cache_k._version:
+        return None
+    pool = st[0]
+    if pool.shape[0] * 128 * D != cache_k.numel() or pool.shape[1] != D:
+        return None
+    return pool
+
+
+def _stash_kpool(cache_k, pool):
+    cache_k._fvb_kpool = (pool, cache_k._version)
+
+
+def _keep_mask(self, dit, q_w, k_w, nh, seqlen, h, w, topk, local_range, pre_cache_k=None):
+    """Block keep mask; returns (keep, pooled keys or None)."""
     D = q_w.shape[-1]
     if getattr(dit, "MASK_RULE", "draft") == "causal":
         per_row = q_w.shape[0] // 128 // seqlen
-        return lcsa.causal_topk_mask(q_w, k_w, nh, per_row, getattr(dit, "CAUSAL_RATIO", 0.25))
+        return lcsa.causal_topk_mask(q_w, k_w, nh, per_row, getattr(dit, "CAUSAL_RATIO", 0.25),
+                                     k_pool_prefix=_cached_kpool(pre_cache_k, D),
+                                     return_k_pool=True)
     local = _local_mask(self, dit, h, w, local_range, q_w.device)
     if _FLAG("FS89_FUSED_MASK", "1"):
-        return lcsa.draft_block_mask(q_w, k_w, nh, seqlen, local, topk)
+        return lcsa.draft_block_mask(q_w, k_w, nh, seqlen, local, topk), None
     m = dit.generate_draft_block_mask(1, nh, seqlen, q_w.view(-1, 128, D), k_w.view(-1, 128, D),
                                       topk=topk, local_attn_mask=local)
-    return m[0] if m.dim() == 4 else m
+    return (m[0] if m.dim() == 4 else m), None
 
 
 def _fast_self_ok(self, x):
@@ -152,25 +221,28 @@ def _fast_self_attn(self, dit, x, freqs, f, h, w, topk, kv_len, pre_cache_k, pre
     nq, nk = _unwrap(self.norm_q), _unwrap(self.norm_k)
     q_w = rms_rope_rows(qkv[:, :D], nq.weight, cos, sin, L, _module_eps(self.norm_q), True, hd,
                         row_map=r2w)
-    k_new = rms_rope_rows(qkv[:, D:2 * D], nk.weight, cos, sin, L, _module_eps(self.norm_k), True,
-                          hd, row_map=r2w)
-    v_new = lcsa.window_partition(qkv[:, 2 * D:], (f, h, w))
     seqlen = f // 2
     one_len = (L // 128) // seqlen
-    if pre_cache_k is not None and pre_cache_v is not None:
-        k_w = torch.cat([pre_cache_k.reshape(-1, D), k_new])
-        v_w = torch.cat([pre_cache_v.reshape(-1, D), v_new])
-    else:
-        k_w, v_w = k_new, v_new
-    keep = _keep_mask(self, dit, q_w, k_w, nh, seqlen, h, w, topk, local_range)
+    nnew = L // 128
+    pk = pre_cache_k if (pre_cache_k is not None and pre_cache_v is not None) else None
+    pv = pre_cache_v if pk is not None else None
+    ark, ak0, ak1 = _arena_slot(pk, nnew, one_len, D, x.device)
+    arv, av0, av1 = _arena_slot(pv, nnew, one_len, D, x.device)
+    # new keys / values land right after the cache: [cache | new] is one contiguous view
+    rms_rope_rows(qkv[:, D:2 * D], nk.weight, cos, sin, L, _module_eps(self.norm_k), True, hd,
+                  out=ark.rows(ak1, ak1 + nnew), row_map=r2w)
+    lcsa.window_partition(qkv[:, 2 * D:], (f, h, w), out=arv.rows(av1, av1 + nnew))
+    k_w, v_w = ark.rows(ak0, ak1 + nnew), arv.rows(av0, av1 + nnew)
+    keep, kpool = _keep_mask(self, dit, q_w, k_w, nh, seqlen, h, w, topk, local_range,
+                             pre_cache_k)
     sel, cnt, _ = lcsa.build_csr(keep)
     o = lcsa.attention_csr(q_w, k_w, v_w, sel, cnt, nh, row_map=w2r)  # raster order
     nkb = k_w.shape[0] // 128
-    kw3, vw3 = k_w.view(nkb, 128, D), v_w.view(nkb, 128, D)
-    if kv_len is not None and nkb // one_len > kv_len:
-        cache_k, cache_v = kw3[one_len:], vw3[one_len:]
-    else:
-        cache_k, cache_v = kw3, vw3
+    drop = one_len if (kv_len is not None and nkb // one_len > kv_len) else 0
+    cache_k = ark.hand_out(ak0 + drop, ak1 + nnew)
+    cache_v = arv.hand_out(av0 + drop, av1 + nnew)
+    if kpool is not None:
+        _stash_kpool(cache_k, kpool[drop:])
     return self.o(o.view(1, L, D)), cache_k, cache_v
 
 

@@ -163,16 +163,50 @@ def draft_block_mask(q_w, k_w, nheads, q_temporal, local, topk, workspace=None):
     return keep
 
 
-def causal_topk_mask(q_w, k_w, nheads, per_row, ratio=0.25, workspace=None):
-    """Benchmark keep rule on the device: own time row + top floor(ratio*#past) past blocks."""
+def block_mean_pool(x_w, out=None):
+    """fp32 mean over each 128-token window (avg_q / avg_k of lcsa/reference.py:41-42):
+    x_w holds nblk windows of 128 rows x C bf16 -> [nblk, C] fp32."""
+    _lib.require_cuda(x_w)
+    C = x_w.shape[-1]
+    nblk = x_w.numel() // (BLOCK * C)
+    if out is None:
+        out = torch.empty((nblk, C), dtype=torch.float32, device=x_w.device)
+    _lib.call("fvb_block_mean_pool", _lib.ptr(x_w.contiguous()), nblk, C, _lib.ptr(out),
+              _lib.stream_of(x_w))
+    return out
+
+
+def causal_topk_mask(q_w, k_w, nheads, per_row, ratio=0.25, workspace=None, k_pool_prefix=None,
+                     return_k_pool=False):
+    """Benchmark keep rule on the device: own time row + top floor(ratio*#past) past blocks.
+
+    k_pool_prefix: pooled fp32 means of the first key blocks (a streaming caller keeps
+    them with its KV cache, since a cached block's mean never changes); only the other
+    key blocks are pooled.  return_k_pool: also return the pooled keys [NK, C].
+    """
     _lib.require_cuda(q_w, k_w)
     C = q_w.shape[-1]
     NQ = q_w.numel() // (BLOCK * C)
     NK = k_w.numel() // (BLOCK * C)
     d = C // nheads
     keep = torch.empty((nheads, NQ, NK), dtype=torch.bool, device=q_w.device)
-    ws = _workspace(_lib.load().fvb_draft_mask_workspace_bytes(nheads, NQ, NK, d), q_w.device, workspace)
-    _lib.call("fvb_causal_topk_mask", _lib.ptr(q_w.contiguous()), _lib.ptr(k_w.contiguous()),
-              nheads, NQ, NK, d, per_row, float(ratio), _lib.ptr(keep.view(torch.uint8)),
-              _lib.ptr(ws), _lib.stream_of(q_w))
-    return keep
+    if k_pool_prefix is None and not return_k_pool:
+        ws = _workspace(_lib.load().fvb_draft_mask_workspace_bytes(nheads, NQ, NK, d), q_w.device,
+                        workspace)
+        _lib.call("fvb_causal_topk_mask", _lib.ptr(q_w.contiguous()), _lib.ptr(k_w.contiguous()),
+                  nheads, NQ, NK, d, per_row, float(ratio), _lib.ptr(keep.view(torch.uint8)),
+                  _lib.ptr(ws), _lib.stream_of(q_w))
+        return keep
+    n0 = 0 if k_pool_prefix is None else k_pool_prefix.shape[0]
+    if n0 > NK or (n0 and tuple(k_pool_prefix.shape) != (n0, C)):
+        raise ValueError(f"causal_topk_mask: k_pool_prefix {tuple(k_pool_prefix.shape)} does not "
+                         f"fit {NK} key blocks of {C} channels")
+    aq = block_mean_pool(q_w)
+    ak = torch.empty((NK, C), dtype=torch.float32, device=q_w.device)
+    if n0:
+        ak[:n0].copy_(k_pool_prefix)
+    if n0 < NK:
+        block_mean_pool(k_w.reshape(-1, C)[n0 * BLOCK:], out=ak[n0:])
+    _lib.call("fvb_causal_topk_pooled", _lib.ptr(aq), _lib.ptr(ak), nheads, NQ, NK, d, per_row,
+              float(ratio), _lib.ptr(keep.view(torch.uint8)), _lib.stream_of(q_w))
+    return (keep, ak) if return_k_pool else keep

@@ -218,6 +218,18 @@ FVB_API int fvb_causal_topk_mask(const void* q_w, const void* k_w, int64_t H, in
                          int64_t d, int64_t per_row, float ratio, uint8_t* keep, void* workspace,
                          fvb_stream_t stream);
 
+/* The two halves of fvb_causal_topk_mask, for callers that keep the pooled means of
+ * cached key blocks (a cached block's mean never changes, so a streaming caller pools
+ * only the new time row).  fvb_block_mean_pool: out[b, c] = fp32 mean over the 128
+ * tokens of window b of x [nblk, 128, C] bf16 (the avg_q / avg_k of
+ * lcsa/reference.py:41-42, kept in fp32).  fvb_causal_topk_pooled: the keep rule above
+ * from pooled aq [NQ, H*d] and ak [NK, H*d] (d % 4 == 0, both 16-byte aligned). */
+FVB_API int fvb_block_mean_pool(const void* x, int64_t nblk, int64_t C, float* out,
+                                fvb_stream_t stream);
+FVB_API int fvb_causal_topk_pooled(const float* aq, const float* ak, int64_t H, int64_t NQ,
+                                   int64_t NK, int64_t d, int64_t per_row, float ratio,
+                                   uint8_t* keep, fvb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

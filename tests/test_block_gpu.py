@@ -42,6 +42,36 @@ def test_block_vs_oracle(mode, monkeypatch):
     assert e < 2e-2 and ek < 2e-2 and ev < 2e-2, (e, ek, ev)
 
 
+def test_streaming_cache_appends_in_place(monkeypatch):
+    """The new key/value row is written after the given cache inside its buffer: results
+    equal the concatenating path (a cache given as fresh tensors), and caches handed out
+    earlier that are still held stay unchanged."""
+    f, h, w = 2, 16, 24
+    P, x, t_mod, ctx, cache = OW.block_case(seed=1, f=f, h=h, w=w)
+    W, dit = build([P], "token", monkeypatch)
+    dit.init_cross_kv(ctx.to(DEV))
+    fr = W.grid_freqs(dit.freqs, f, h, w, f0=6).to(DEV)
+    blk = dit.blocks[0]
+    x2 = (x.float().flip(1)).to(torch.bfloat16).to(DEV)
+
+    def run(xx, ck, cv):
+        return blk(xx, None, t_mod.to(DEV), fr, f, h, w, kv_len=3, is_stream=True,
+                   pre_cache_k=ck, pre_cache_v=cv)
+
+    with torch.no_grad():
+        y1, ck1, cv1 = run(x.to(DEV), cache[0].to(DEV), cache[1].to(DEV))
+        snap1 = (ck1.clone(), cv1.clone())
+        y2, ck2, cv2 = run(x2, ck1, cv1)  # appended in place after ck1
+        y2c, ck2c, cv2c = run(x2, ck1.clone(), cv1.clone())  # copied into a new buffer
+        assert torch.equal(y2, y2c) and torch.equal(ck2, ck2c) and torch.equal(cv2, cv2c)
+        assert torch.equal(ck1, snap1[0]) and torch.equal(cv1, snap1[1])
+        snap2 = (ck2.clone(), cv2.clone())
+        y3, ck3, cv3 = run(x2, ck1, cv1)  # ck2 still held: its windows must not be reused
+        assert torch.equal(y3, y2)
+        assert torch.equal(ck2, snap2[0]) and torch.equal(cv2, snap2[1])
+        assert torch.equal(ck3, ck2) and torch.equal(cv3, cv2)
+
+
 def test_draft_mask_rule_block(monkeypatch):
     """The FlashVSR selection (local window + joint top-k) on the device builder."""
     f, h, w, heads = 2, 16, 24, 12

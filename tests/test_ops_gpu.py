@@ -383,3 +383,9 @@ def test_causal_topk_mask_device():
     ref = O.causal_topk_mask(q_w, k_w, H, 66, 0.25)
     assert keep.sum().item() == 12 * (66 * 66 + 66 * 82)  # the configuration's kept pairs
     assert (keep == ref).float().mean().item() > 0.999
+    # the streaming split: pooled means of the cached key blocks passed in, the rest pooled
+    keep2, ak = causal_topk_mask(q_w.to(DEV), k_w.to(DEV), H, 66, 0.25, return_k_pool=True)
+    assert torch.equal(keep2.cpu(), keep)
+    torch.testing.assert_close(ak.cpu(), k_w.float().mean(dim=1), rtol=1e-5, atol=1e-6)
+    keep3 = causal_topk_mask(q_w.to(DEV), k_w.to(DEV), H, 66, 0.25, k_pool_prefix=ak[:66].clone())
+    assert torch.equal(keep3.cpu(), keep)
