@@ -51,6 +51,10 @@ _SIGS = {
     "fvb_rms_rope": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _int, _vp, _vp, _vp]),
     "fvb_ln_modulate": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp, _vp, _vp]),
     "fvb_layer_norm": (_int, [_vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp, _vp]),
+    "fvb_gate_add_ln_modulate": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp,
+                                         _vp, _vp, _vp]),
+    "fvb_gate_add_layer_norm": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp,
+                                        _vp, _vp, _vp]),
     "fvb_gate_add": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "fvb_mask_to_csr": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "fvb_bsa_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp]),

@@ -64,6 +64,30 @@ __device__ __forceinline__ float bf16r(float x) {  // round-trip through bf16 (R
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// packed fp32x2 arithmetic (sm_100): two lanes of work per instruction
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 // fp32 -> e4m3 (round to nearest even, saturating to +-448): the rounding the
 // reference gets from Triton's `.to(tl.float8e4nv)` after an explicit clamp.
 __device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
@@ -86,34 +110,41 @@ __device__ __forceinline__ float gelu_tanh_bf16(float x) {
   return bf16r(0.5f * x * (1.0f + tanhf(inner)));
 }
 
-// x / s as the e4m3 conversion sees it, without a full IEEE divide in the common case.
-// rs = 1/s correctly rounded.  y = x * rs is within 2 fp32 ulps of the IEEE quotient
-// __fdiv_rn(x, s); their e4m3 roundings (3 mantissa bits kept, round to nearest even) can
-// only differ when y lies within a few ulps of an e4m3 rounding midpoint (fp32 mantissa low
-// 20 bits == 0x80000) or in the e4m3 subnormal range (|y| < 2^-6).  Those inputs must take
-// the exact divide, so the resulting code always equals e4m3(__fdiv_rn(x, s)).
-__device__ __forceinline__ bool e4m3_needs_exact(float y) {
-  const uint32_t b = __float_as_uint(y) & 0x7fffffffu;
-  return ((b & 0xFFFFFu) - 0x80000u + 8u) < 16u || b < 0x3C800000u /* 2^-6 */;
-}
-
-__device__ __noinline__ uint32_t e4m3x2_exact(float x0, float x1, float s) {
-  return f32x2_to_e4m3x2(__fdiv_rn(x0, s), __fdiv_rn(x1, s));
+__device__ __noinline__ uint2 e4m3x8_exact(float f0, float f1, float f2, float f3, float f4,
+                                           float f5, float f6, float f7, float s) {
+  const uint32_t c0 = f32x2_to_e4m3x2(__fdiv_rn(f0, s), __fdiv_rn(f1, s));
+  const uint32_t c1 = f32x2_to_e4m3x2(__fdiv_rn(f2, s), __fdiv_rn(f3, s));
+  const uint32_t c2 = f32x2_to_e4m3x2(__fdiv_rn(f4, s), __fdiv_rn(f5, s));
+  const uint32_t c3 = f32x2_to_e4m3x2(__fdiv_rn(f6, s), __fdiv_rn(f7, s));
+  return make_uint2(c0 | (c1 << 16), c2 | (c3 << 16));
 }
 
 // 8 fp32 values -> 8 e4m3 codes of clamp(x / s, +-448), rounded to nearest even, packed in
-// a uint2 (the quantisation of fp8_quant.py:16-35).  rs = __frcp_rn(s), hoisted by the
-// caller.  The saturating conversion is the clamp (finite values beyond +-448 go to +-448,
-// NaN stays NaN as clamp-then-cast leaves it).  A pair with a product x * rs that may
-// round differently from the IEEE quotient takes the exact divide (out of line: rare).
+// a uint2 (the quantisation of fp8_quant.py:16-35), without an IEEE divide in the common
+// case.  rs = __frcp_rn(s), hoisted by the caller.  The saturating conversion is the clamp
+// (finite values beyond +-448 go to +-448, NaN stays NaN as clamp-then-cast leaves it).
+// x * rs(1 - 2^-20) and x * rs(1 + 2^-20), each rounded, bracket the IEEE quotient
+// fl(x / s) (their relative distance from x / s exceeds 2^-21 after all roundings, the
+// quotient's is at most 2^-24; below the fp32 normal range every value involved converts
+// to a signed zero).  The conversion is monotone, so when both ends give the same code the
+// quotient does too.  If any of the 8 values fails that test (a rounding boundary inside
+// its bracket), all 8 take the exact divide (out of line: rare).
 __device__ __forceinline__ uint2 e4m3_codes8(const float* f, float s, float rs) {
+  const uint64_t lo2 = f2_pack(rs * 0.99999904632568359375f, rs * 0.99999904632568359375f);
+  const uint64_t hi2 = f2_pack(rs * 1.00000095367431640625f, rs * 1.00000095367431640625f);
   uint32_t c[4];
+  bool exact = false;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float y0 = f[2 * i] * rs, y1 = f[2 * i + 1] * rs;
-    c[i] = (e4m3_needs_exact(y0) | e4m3_needs_exact(y1)) ? e4m3x2_exact(f[2 * i], f[2 * i + 1], s)
-                                                          : f32x2_to_e4m3x2(y0, y1);
+    const uint64_t x2 = f2_pack(f[2 * i], f[2 * i + 1]);
+    float a0, a1, b0, b1;
+    f2_unpack(f2_mul(x2, lo2), a0, a1);
+    f2_unpack(f2_mul(x2, hi2), b0, b1);
+    const uint16_t lo = f32x2_to_e4m3x2(a0, a1), hi = f32x2_to_e4m3x2(b0, b1);
+    exact |= lo != hi;
+    c[i] = lo;
   }
+  if (exact) return e4m3x8_exact(f[0], f[1], f[2], f[3], f[4], f[5], f[6], f[7], s);
   return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
 }
 
@@ -180,6 +211,24 @@ __device__ __forceinline__ void row_pipeline(int64_t rows, Load load, Body body)
     body(row, cur);
 #pragma unroll
     for (int j = 0; j < NV; ++j) cur[j] = nxt[j];
+  }
+}
+
+// The same schedule for rows that are combined from NL raw vectors per lane (e.g. a row
+// and the residual added to it): prep(row, raw, cur) turns the arrived raw vectors into the
+// row's NV working vectors before the next row's raw loads are issued into the same
+// registers, so a lane holds NL + NV vectors instead of 2 * NL.
+template <int NV, int NL, typename Load, typename Prep, typename Body>
+__device__ __forceinline__ void row_pipeline_prep(int64_t rows, Load load, Prep prep, Body body) {
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  uint4 raw[NL], cur[NV];
+  load(row, raw);
+  for (; row < rows; row += nwarps) {
+    prep(row, raw, cur);
+    if (row + nwarps < rows) load(row + nwarps, raw);
+    body(row, cur);
   }
 }
 
@@ -397,30 +446,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// packed fp32x2 arithmetic (sm_100): two lanes of work per instruction
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
-  asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {  // sm_100 3-input max
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));

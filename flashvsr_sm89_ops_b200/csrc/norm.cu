@@ -32,6 +32,34 @@ __device__ __forceinline__ uint2 fp8_codes8(const uint4& y, float qs, float rqs)
   return e4m3_codes8(f, qs, rqs);
 }
 
+// Gated residual add of one row held in registers (the gate_add_kernel arithmetic):
+// x <- bf16(x + bf16(g * r)) (g == nullptr: bf16(x + r)), also stored to xo; raw holds
+// the row's x vectors then its r vectors.
+template <int NV>
+__device__ __forceinline__ void gate_add_row(const uint4* raw, uint4* xr, int lane, int nvec,
+                                             const __nv_bfloat16* g, uint4* xo) {
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int v = j * 32 + lane;
+    if (v < nvec) {
+      float xf[8], rf[8];
+      bf16x8_to_f32(raw[j], xf);
+      bf16x8_to_f32(raw[NV + j], rf);
+      if (g) {
+        float gf[8];
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(g) + v), gf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xf[i] = xf[i] + bf16r(gf[i] * rf[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xf[i] = xf[i] + rf[i];
+      }
+      xr[j] = f32_to_bf16x8(xf);
+      xo[v] = xr[j];
+    }
+  }
+}
+
 // Row mean and (x - mean) * rden with rden = 1/sqrt(var + eps), two-pass in registers.
 // x holds NV 16-byte vectors per lane (bf16); sums use packed fp32 pairs.
 template <int NV>
@@ -76,11 +104,16 @@ __device__ __forceinline__ void row_stats(const uint4* xr, int lane, int nvec, i
 // rounding in the reference; the packed bf16x2 instructions (non-contracting _rn forms) round
 // the exact result once, which is the same value (fp32 carries more than twice bf16's
 // precision plus two bits, so the fp32 intermediate never changes a bf16 rounding).
-template <bool EMIT_FP8, int NV>
-__global__ void __launch_bounds__(256, kRowBlocksPerSM) ln_modulate_kernel(
-    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ scale,
-    const __nv_bfloat16* __restrict__ shift, int64_t rows, int64_t L, int D, float eps,
-    __nv_bfloat16* __restrict__ out, uint8_t* __restrict__ q8, float* __restrict__ q_scale) {
+// GATE: the row is first the gated residual sum x + g * r of gate_add_kernel (stored to
+// x_out), so the add and the norm that follows it read the residual stream once.  out may
+// be nullptr when only the FP8 codes are consumed.
+template <bool EMIT_FP8, int NV, bool GATE>
+__global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ gate,
+    const __nv_bfloat16* __restrict__ r, __nv_bfloat16* __restrict__ x_out,
+    const __nv_bfloat16* __restrict__ scale, const __nv_bfloat16* __restrict__ shift,
+    int64_t rows, int64_t L, int D, float eps, __nv_bfloat16* __restrict__ out,
+    uint8_t* __restrict__ q8, float* __restrict__ q_scale) {
   const int lane = threadIdx.x & 31;
   const int nvec = D >> 3;
   auto load = [&](int64_t row, uint4* xr) {
@@ -88,6 +121,12 @@ __global__ void __launch_bounds__(256, kRowBlocksPerSM) ln_modulate_kernel(
 #pragma unroll
     for (int j = 0; j < NV; ++j)
       if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+    if (GATE) {
+      const uint4* rv = reinterpret_cast<const uint4*>(r + row * D);
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+        if (j * 32 + lane < nvec) xr[NV + j] = __ldg(rv + j * 32 + lane);
+    }
   };
   auto body = [&](int64_t row, uint4* xr) {
     const int64_t b = row / L;
@@ -121,7 +160,7 @@ __global__ void __launch_bounds__(256, kRowBlocksPerSM) ln_modulate_kernel(
           y2[p] = y;
           if (EMIT_FP8) m2 = __hmax2(m2, __habs2(y));
         }
-        ov[v] = yo;
+        if (out) ov[v] = yo;
         xr[j] = yo;
       }
     }
@@ -139,17 +178,30 @@ __global__ void __launch_bounds__(256, kRowBlocksPerSM) ln_modulate_kernel(
       if (lane == 0) q_scale[row] = __fdiv_rn(amax, 448.0f);
     }
   };
-  row_pipeline<NV>(rows, load, body);
+  if (GATE) {
+    auto prep = [&](int64_t row, const uint4* raw, uint4* xr) {
+      gate_add_row<NV>(raw, xr, lane, nvec, gate ? gate + (row / L) * D : nullptr,
+                       reinterpret_cast<uint4*>(x_out + row * D));
+    };
+    row_pipeline_prep<NV, 2 * NV>(rows, load, prep, body);
+  } else {
+    row_pipeline<NV>(rows, load, body);
+  }
 }
 
 // LayerNorm with optional affine weight / bias, fp32 math and one bf16 rounding (the
-// semantics of torch.nn.LayerNorm on bf16 tensors); optionally also the per-token e4m3
-// codes of that bf16 output (what the next FP8 linear would compute from it).
-template <bool EMIT_FP8, int NV>
+// semantics of torch.nn.LayerNorm on bf16 tensors; the affine step is one fused
+// multiply-add per element); optionally also the per-token e4m3 codes of that bf16 output
+// (what the next FP8 linear would compute from it).
+// GATE: as for ln_modulate_kernel, the row is first x + g * r (stored to x_out; the gate
+// row of batch item row / L).
+template <bool EMIT_FP8, int NV, bool GATE>
 __global__ void __launch_bounds__(256, 2) layer_norm_kernel(
-    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
-    const __nv_bfloat16* __restrict__ bias, int64_t rows, int D, float eps,
-    __nv_bfloat16* __restrict__ out, uint8_t* __restrict__ q8, float* __restrict__ q_scale) {
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ gate,
+    const __nv_bfloat16* __restrict__ r, __nv_bfloat16* __restrict__ x_out, int64_t L,
+    const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ bias, int64_t rows,
+    int D, float eps, __nv_bfloat16* __restrict__ out, uint8_t* __restrict__ q8,
+    float* __restrict__ q_scale) {
   const int lane = threadIdx.x & 31;
   const int nvec = D >> 3;
   auto load = [&](int64_t row, uint4* xr) {
@@ -157,11 +209,18 @@ __global__ void __launch_bounds__(256, 2) layer_norm_kernel(
 #pragma unroll
     for (int j = 0; j < NV; ++j)
       if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+    if (GATE) {
+      const uint4* rv = reinterpret_cast<const uint4*>(r + row * D);
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+        if (j * 32 + lane < nvec) xr[NV + j] = __ldg(rv + j * 32 + lane);
+    }
   };
   auto body = [&](int64_t row, uint4* xr) {
     float mean, rstd;
     row_stats<NV>(xr, lane, nvec, D, eps, mean, rstd);
-    float amax = 0.f;
+    const uint64_t nm = f2_pack(-mean, -mean), rs2 = f2_pack(rstd, rstd);
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
     uint4* ov = reinterpret_cast<uint4*>(out + row * D);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
@@ -171,26 +230,30 @@ __global__ void __launch_bounds__(256, 2) layer_norm_kernel(
         bf16x8_to_f32(xr[j], f);
         if (w) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), ww);
         if (bias) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(bias) + v), bb);
+        uint4 yo;
+        __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&yo);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float y = (f[i] - mean) * rstd;
-          if (w) y = y * ww[i];
-          if (bias) y = y + bb[i];
-          f[i] = y;
+        for (int p = 0; p < 4; ++p) {
+          // (x - mean) * rstd, then * w + b (one fused multiply-add), in fp32 pairs
+          uint64_t y = f2_mul(f2_add(f2_pack(f[2 * p], f[2 * p + 1]), nm), rs2);
+          if (w && bias)
+            y = f2_fma(y, f2_pack(ww[2 * p], ww[2 * p + 1]), f2_pack(bb[2 * p], bb[2 * p + 1]));
+          else if (w)
+            y = f2_mul(y, f2_pack(ww[2 * p], ww[2 * p + 1]));
+          else if (bias)
+            y = f2_add(y, f2_pack(bb[2 * p], bb[2 * p + 1]));
+          float a, c;
+          f2_unpack(y, a, c);
+          y2[p] = __floats2bfloat162_rn(a, c);
+          if (EMIT_FP8) m2 = __hmax2(m2, __habs2(y2[p]));
         }
-        const uint4 yo = f32_to_bf16x8(f);
-        ov[v] = yo;
-        if (EMIT_FP8) {
-          float r[8];
-          bf16x8_to_f32(yo, r);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(r[i]));
-          xr[j] = yo;
-        }
+        if (out) ov[v] = yo;
+        if (EMIT_FP8) xr[j] = yo;
       }
     }
     if (EMIT_FP8) {
-      amax = warp_max(amax);
+      const float2 mf = __bfloat1622float2(m2);
+      const float amax = warp_max(fmaxf(mf.x, mf.y));
       const float qs = quant_scale_from_amax_n(amax);
       const float rqs = __frcp_rn(qs);
       uint2* qv = reinterpret_cast<uint2*>(q8 + row * D);
@@ -202,7 +265,15 @@ __global__ void __launch_bounds__(256, 2) layer_norm_kernel(
       if (lane == 0) q_scale[row] = __fdiv_rn(amax, 448.0f);
     }
   };
-  row_pipeline<NV>(rows, load, body);
+  if (GATE) {
+    auto prep = [&](int64_t row, const uint4* raw, uint4* xr) {
+      gate_add_row<NV>(raw, xr, lane, nvec, gate ? gate + (row / L) * D : nullptr,
+                       reinterpret_cast<uint4*>(x_out + row * D));
+    };
+    row_pipeline_prep<NV, 2 * NV>(rows, load, prep, body);
+  } else {
+    row_pipeline<NV>(rows, load, body);
+  }
 }
 
 __global__ void __launch_bounds__(256) gate_add_kernel(const uint4* __restrict__ x,
@@ -324,6 +395,64 @@ static void dispatch_nv(int64_t D, F&& f) {
   else f(std::integral_constant<int, 8>{});
 }
 
+// Shared host paths of the plain and the gated-residual entry points (r == nullptr: plain).
+// out may be nullptr when q8 is given (only the FP8 codes are consumed).
+static int ln_modulate_impl(const void* x, const void* gate, const void* r, void* x_out,
+                            const void* scale, const void* shift, int64_t B, int64_t L, int64_t D,
+                            float eps, void* out, void* q8, float* q_scale, fvb_stream_t stream,
+                            const char* name) {
+  const int64_t rows = B * L;
+  FVB_REQUIRE(x && scale && shift && (out || q8), "%s: NULL pointer", name);
+  FVB_REQUIRE(aligned16(x) && aligned16(scale) && aligned16(shift) && (!out || aligned16(out)),
+              "%s: pointers must be 16-byte aligned", name);
+  if (q8) FVB_REQUIRE((reinterpret_cast<uintptr_t>(q8) & 7u) == 0, "%s: q8 alignment", name);
+  auto launch = [&](auto emit, auto nv, auto gated) {
+    ln_modulate_kernel<decltype(emit)::value, decltype(nv)::value, decltype(gated)::value>
+        <<<row_grid(rows, gated ? 2 : kRowBlocksPerSM), 256, 0, (cudaStream_t)stream>>>(
+            (const __nv_bfloat16*)x, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)r,
+            (__nv_bfloat16*)x_out, (const __nv_bfloat16*)scale, (const __nv_bfloat16*)shift, rows,
+            L, (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
+  };
+  dispatch_nv(D, [&](auto nv) {
+    if (r) {
+      if (q8) launch(std::true_type{}, nv, std::true_type{});
+      else launch(std::false_type{}, nv, std::true_type{});
+    } else {
+      if (q8) launch(std::true_type{}, nv, std::false_type{});
+      else launch(std::false_type{}, nv, std::false_type{});
+    }
+  });
+  return check_launch(name);
+}
+
+static int layer_norm_impl(const void* x, const void* gate, const void* r, void* x_out, int64_t L,
+                           int64_t rows, const void* w, const void* b, int64_t D, float eps,
+                           void* out, void* q8, float* q_scale, fvb_stream_t stream,
+                           const char* name) {
+  FVB_REQUIRE(x && (out || q8), "%s: NULL pointer", name);
+  FVB_REQUIRE(aligned16(x) && (!out || aligned16(out)) && (!w || aligned16(w)) &&
+                  (!b || aligned16(b)),
+              "%s: pointers must be 16-byte aligned", name);
+  if (q8) FVB_REQUIRE((reinterpret_cast<uintptr_t>(q8) & 7u) == 0, "%s: q8 alignment", name);
+  auto launch = [&](auto emit, auto nv, auto gated) {
+    layer_norm_kernel<decltype(emit)::value, decltype(nv)::value, decltype(gated)::value>
+        <<<row_grid(rows, 2), 256, 0, (cudaStream_t)stream>>>(
+            (const __nv_bfloat16*)x, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)r,
+            (__nv_bfloat16*)x_out, L, (const __nv_bfloat16*)w, (const __nv_bfloat16*)b, rows,
+            (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
+  };
+  dispatch_nv(D, [&](auto nv) {
+    if (r) {
+      if (q8) launch(std::true_type{}, nv, std::true_type{});
+      else launch(std::false_type{}, nv, std::true_type{});
+    } else {
+      if (q8) launch(std::true_type{}, nv, std::false_type{});
+      else launch(std::false_type{}, nv, std::false_type{});
+    }
+  });
+  return check_launch(name);
+}
+
 }  // namespace fvb
 
 extern "C" {
@@ -335,23 +464,26 @@ int fvb_ln_modulate(const void* x, const void* scale, const void* shift, int64_t
   FVB_REQUIRE(B >= 0 && L >= 0 && D > 0, "fvb_ln_modulate: bad shape");
   FVB_REQUIRE(D % 8 == 0 && D <= 2048, "fvb_ln_modulate: D must be a multiple of 8, <= 2048");
   FVB_REQUIRE((q8 == nullptr) == (q_scale == nullptr), "fvb_ln_modulate: q8/q_scale go together");
-  const int64_t rows = B * L;
-  if (rows == 0) return FVB_OK;
-  FVB_REQUIRE(x && scale && shift && out, "fvb_ln_modulate: NULL pointer");
-  FVB_REQUIRE(aligned16(x) && aligned16(scale) && aligned16(shift) && aligned16(out),
-              "fvb_ln_modulate: pointers must be 16-byte aligned");
-  if (q8) FVB_REQUIRE((reinterpret_cast<uintptr_t>(q8) & 7u) == 0, "fvb_ln_modulate: q8 alignment");
-  auto launch = [&](auto emit, auto nv) {
-    ln_modulate_kernel<decltype(emit)::value, decltype(nv)::value>
-        <<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
-            (const __nv_bfloat16*)x, (const __nv_bfloat16*)scale, (const __nv_bfloat16*)shift,
-            rows, L, (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
-  };
-  dispatch_nv(D, [&](auto nv) {
-    if (q8) launch(std::true_type{}, nv);
-    else launch(std::false_type{}, nv);
-  });
-  return check_launch("fvb_ln_modulate");
+  if (B * L == 0) return FVB_OK;
+  return ln_modulate_impl(x, nullptr, nullptr, nullptr, scale, shift, B, L, D, eps, out, q8,
+                          q_scale, stream, "fvb_ln_modulate");
+}
+
+int fvb_gate_add_ln_modulate(const void* x, const void* gate, const void* r, void* x_out,
+                             const void* scale, const void* shift, int64_t B, int64_t L, int64_t D,
+                             float eps, void* out, void* q8, float* q_scale, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(B >= 0 && L >= 0 && D > 0, "fvb_gate_add_ln_modulate: bad shape");
+  FVB_REQUIRE(D % 8 == 0 && D <= 2048,
+              "fvb_gate_add_ln_modulate: D must be a multiple of 8, <= 2048");
+  FVB_REQUIRE((q8 == nullptr) == (q_scale == nullptr),
+              "fvb_gate_add_ln_modulate: q8/q_scale go together");
+  if (B * L == 0) return FVB_OK;
+  FVB_REQUIRE(r && x_out && aligned16(r) && aligned16(x_out) && (!gate || aligned16(gate)),
+              "fvb_gate_add_ln_modulate: r / x_out / gate NULL or not 16-byte aligned");
+  FVB_REQUIRE(x_out != x && x_out != r, "fvb_gate_add_ln_modulate: x_out must not alias x or r");
+  return ln_modulate_impl(x, gate, r, x_out, scale, shift, B, L, D, eps, out, q8, q_scale, stream,
+                          "fvb_gate_add_ln_modulate");
 }
 
 int fvb_layer_norm(const void* x, const void* w, const void* b, int64_t rows, int64_t D,
@@ -360,21 +492,24 @@ int fvb_layer_norm(const void* x, const void* w, const void* b, int64_t rows, in
   FVB_REQUIRE(rows >= 0 && D > 0 && D % 8 == 0 && D <= 2048, "fvb_layer_norm: bad shape");
   FVB_REQUIRE((q8 == nullptr) == (q_scale == nullptr), "fvb_layer_norm: q8/q_scale go together");
   if (rows == 0) return FVB_OK;
-  FVB_REQUIRE(x && out, "fvb_layer_norm: NULL pointer");
-  FVB_REQUIRE(aligned16(x) && aligned16(out) && (!w || aligned16(w)) && (!b || aligned16(b)),
-              "fvb_layer_norm: pointers must be 16-byte aligned");
-  if (q8) FVB_REQUIRE((reinterpret_cast<uintptr_t>(q8) & 7u) == 0, "fvb_layer_norm: q8 alignment");
-  auto launch = [&](auto emit, auto nv) {
-    layer_norm_kernel<decltype(emit)::value, decltype(nv)::value>
-        <<<row_grid(rows, 2), 256, 0, (cudaStream_t)stream>>>(
-            (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (const __nv_bfloat16*)b, rows,
-            (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
-  };
-  dispatch_nv(D, [&](auto nv) {
-    if (q8) launch(std::true_type{}, nv);
-    else launch(std::false_type{}, nv);
-  });
-  return check_launch("fvb_layer_norm");
+  return layer_norm_impl(x, nullptr, nullptr, nullptr, 1, rows, w, b, D, eps, out, q8, q_scale,
+                         stream, "fvb_layer_norm");
+}
+
+int fvb_gate_add_layer_norm(const void* x, const void* gate, const void* r, void* x_out,
+                            const void* w, const void* b, int64_t B, int64_t L, int64_t D,
+                            float eps, void* out, void* q8, float* q_scale, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(B >= 0 && L >= 0 && D > 0 && D % 8 == 0 && D <= 2048,
+              "fvb_gate_add_layer_norm: bad shape");
+  FVB_REQUIRE((q8 == nullptr) == (q_scale == nullptr),
+              "fvb_gate_add_layer_norm: q8/q_scale go together");
+  if (B * L == 0) return FVB_OK;
+  FVB_REQUIRE(r && x_out && aligned16(r) && aligned16(x_out) && (!gate || aligned16(gate)),
+              "fvb_gate_add_layer_norm: r / x_out / gate NULL or not 16-byte aligned");
+  FVB_REQUIRE(x_out != x && x_out != r, "fvb_gate_add_layer_norm: x_out must not alias x or r");
+  return layer_norm_impl(x, gate, r, x_out, L, B * L, w, b, D, eps, out, q8, q_scale, stream,
+                         "fvb_gate_add_layer_norm");
 }
 
 int fvb_gate_add(const void* x, const void* gate, const void* r, int64_t B, int64_t L,

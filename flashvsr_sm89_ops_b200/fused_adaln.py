@@ -21,8 +21,13 @@ def _check(x, name):
 
 
 def fused_ln_modulate(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
-                      eps: float = 1e-6, emit_fp8: bool = False, out: torch.Tensor | None = None):
-    """LayerNorm(affine=False) + modulate. x [B, L, D] contiguous bf16; scale/shift [B, 1, D]."""
+                      eps: float = 1e-6, emit_fp8: bool = False, out: torch.Tensor | None = None,
+                      want_out: bool = True):
+    """LayerNorm(affine=False) + modulate. x [B, L, D] contiguous bf16; scale/shift [B, 1, D].
+
+    emit_fp8=True also returns the output's per-token FP8 codes and scales:
+    (out, q8, scale); want_out=False (with emit_fp8) skips the bf16 output (returned None).
+    """
     _check(x, "fused_ln_modulate")
     B, L, D = x.shape
     assert x.is_contiguous() and scale.is_contiguous() and shift.is_contiguous()
@@ -30,7 +35,9 @@ def fused_ln_modulate(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
         raise ValueError("fused_ln_modulate: scale/shift must be bf16")
     if scale.numel() != B * D or shift.numel() != B * D:
         raise ValueError("fused_ln_modulate: scale/shift must be [B, 1, D]")
-    if out is None:
+    if not want_out and not emit_fp8:
+        raise ValueError("fused_ln_modulate: want_out=False needs emit_fp8=True")
+    if out is None and want_out:
         out = torch.empty_like(x)
     q8 = qs = None
     if emit_fp8:
@@ -56,6 +63,54 @@ def fused_gate_add(x: torch.Tensor, gate: torch.Tensor | None, residual: torch.T
     _lib.call("fvb_gate_add", _lib.ptr(x), _lib.ptr(gate), _lib.ptr(residual), B, L, D,
               _lib.ptr(out), _lib.stream_of(x))
     return out
+
+
+def _fp8_bufs(rows, D, device):
+    return (torch.empty((rows, D), dtype=torch.float8_e4m3fn, device=device),
+            torch.empty((rows,), dtype=torch.float32, device=device))
+
+
+def gate_add_ln_modulate(x, gate, residual, scale, shift, eps=1e-6, emit_fp8=False,
+                         want_out=True):
+    """fused_gate_add(x, gate, residual) followed by fused_ln_modulate of its result, in one
+    pass over the residual stream (bitwise the two calls).  gate [B, 1, D] or None.
+    Returns (x_new, out) or, with emit_fp8, (x_new, out, q8, scale); out is None when
+    want_out=False."""
+    _check(x, "gate_add_ln_modulate")
+    B, L, D = x.shape
+    for t in (x, residual, scale, shift) + ((gate,) if gate is not None else ()):
+        if not t.is_contiguous() or t.dtype != torch.bfloat16:
+            raise ValueError("gate_add_ln_modulate: tensors must be contiguous bf16")
+    if not want_out and not emit_fp8:
+        raise ValueError("gate_add_ln_modulate: want_out=False needs emit_fp8=True")
+    x_new = torch.empty_like(x)
+    out = torch.empty_like(x) if want_out else None
+    q8, qs = _fp8_bufs(B * L, D, x.device) if emit_fp8 else (None, None)
+    _lib.call("fvb_gate_add_ln_modulate", _lib.ptr(x), _lib.ptr(gate), _lib.ptr(residual),
+              _lib.ptr(x_new), _lib.ptr(scale), _lib.ptr(shift), B, L, D, float(eps),
+              _lib.ptr(out), _lib.ptr(q8), _lib.ptr(qs), _lib.stream_of(x))
+    return (x_new, out, q8, qs) if emit_fp8 else (x_new, out)
+
+
+def gate_add_layer_norm(x, gate, residual, weight, bias, eps=1e-6, emit_fp8=False, want_out=True):
+    """fused_gate_add(x, gate, residual) followed by layer_norm(weight, bias) of its result,
+    in one pass (bitwise the two calls).  Returns as gate_add_ln_modulate."""
+    _check(x, "gate_add_layer_norm")
+    B, L, D = x.shape
+    for t in (x, residual) + ((gate,) if gate is not None else ()):
+        if not t.is_contiguous() or t.dtype != torch.bfloat16:
+            raise ValueError("gate_add_layer_norm: tensors must be contiguous bf16")
+    if not want_out and not emit_fp8:
+        raise ValueError("gate_add_layer_norm: want_out=False needs emit_fp8=True")
+    w = weight.to(torch.bfloat16).contiguous() if weight is not None else None
+    b = bias.to(torch.bfloat16).contiguous() if bias is not None else None
+    x_new = torch.empty_like(x)
+    out = torch.empty_like(x) if want_out else None
+    q8, qs = _fp8_bufs(B * L, D, x.device) if emit_fp8 else (None, None)
+    _lib.call("fvb_gate_add_layer_norm", _lib.ptr(x), _lib.ptr(gate), _lib.ptr(residual),
+              _lib.ptr(x_new), _lib.ptr(w), _lib.ptr(b), B, L, D, float(eps), _lib.ptr(out),
+              _lib.ptr(q8), _lib.ptr(qs), _lib.stream_of(x))
+    return (x_new, out, q8, qs) if emit_fp8 else (x_new, out)
 
 
 def layer_norm(x: torch.Tensor, weight: torch.Tensor | None, bias: torch.Tensor | None,

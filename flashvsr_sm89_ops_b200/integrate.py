@@ -33,7 +33,8 @@ from .compat_bsa import active_backend, ensure_bsa_available
 from .fp8_ffn import FP8FFN, convert_ffn_fp8, ffn_fp8
 from .fp8_linear import FP8Linear, convert_linears_fp8, fp8_mm
 from .fp8_quant import default_act_mode, quantize_fp8
-from .fused_adaln import fused_gate_add, fused_ln_modulate, layer_norm
+from .fused_adaln import (fused_gate_add, fused_ln_modulate, gate_add_layer_norm,
+                          gate_add_ln_modulate, layer_norm)
 from .fused_rms_rope import freqs_cos_sin, fused_rms_rope, rms_rope_rows
 
 
@@ -201,6 +202,17 @@ def _fast_self_ok(self, x):
         and _qkv_pack(self) is not None and type(self.o) is FP8Linear
 
 
+def _self_fast_path(dit, attn, x):
+    """Whether attn's forward takes the B200 fast path for input shaped like x."""
+    return getattr(dit, "FUSED_ROPE_FN", None) is fused_rms_rope and _fast_self_ok(attn, x)
+
+
+def _cross_fast_path(dit, ca, x):
+    """Whether the cross-attention forward takes the B200 fast path for input like x."""
+    return getattr(dit, "FUSED_ROPE_FN", None) is fused_rms_rope and x.dim() == 3 \
+        and x.shape[0] == 1 and x.is_cuda and type(ca.q) is FP8Linear and type(ca.o) is FP8Linear
+
+
 # ----------------------------------------------------------------------------- forwards
 def _fast_self_attn(self, dit, x, freqs, f, h, w, topk, kv_len, pre_cache_k, pre_cache_v,
                     local_range):
@@ -260,7 +272,7 @@ def _make_self_attn_forward(dit):
         assert L == f * h * w, "Sequence length mismatch with provided (f,h,w)."
 
         rope_fn = getattr(dit, "FUSED_ROPE_FN", None)
-        if rope_fn is fused_rms_rope and _fast_self_ok(self, x):
+        if _self_fast_path(dit, self, x):
             out, ck, cv = _fast_self_attn(self, dit, x, freqs, f, h, w, topk, kv_len,
                                           pre_cache_k, pre_cache_v, local_range)
             return (out, ck, cv) if is_stream else out
@@ -311,8 +323,7 @@ def _make_cross_attn_forward(dit):
     def forward(self, x, y, is_stream=False):
         rope_fn = getattr(dit, "FUSED_ROPE_FN", None)
         assert self.cache_k is not None and self.cache_v is not None
-        if rope_fn is fused_rms_rope and x.dim() == 3 and x.shape[0] == 1 and x.is_cuda \
-                and type(self.q) is FP8Linear and type(self.o) is FP8Linear:
+        if _cross_fast_path(dit, self, x):
             _, L, D = x.shape
             pre = _take_stash(self, x)
             if pre is None:
@@ -346,8 +357,13 @@ def _make_dit_block_forward(dit):
         if fa is not None:
             ln_mod, gate_add = fa
             if token and _qkv_pack(self.self_attn) is not None and self.self_attn.q.mode == "token":
+                # the fast self-attention path reads only the FP8 codes: no bf16 output then
+                # (the block input stands in for it as the stash key)
+                skip = _self_fast_path(dit, self.self_attn, x)
                 input_x, x8, s8 = fused_ln_modulate(x, scale_msa, shift_msa,
-                                                    eps=_module_eps(self.norm1), emit_fp8=True)
+                                                    eps=_module_eps(self.norm1), emit_fp8=True,
+                                                    want_out=not skip)
+                input_x = x if input_x is None else input_x
                 self.self_attn._fvb_x8 = (input_x, x8.view(-1, x.shape[-1]), s8)
             else:
                 input_x = ln_mod(x, scale_msa, shift_msa, eps=_module_eps(self.norm1))
@@ -357,31 +373,42 @@ def _make_dit_block_forward(dit):
             input_x, freqs, f, h, w, local_num, topk, train_img, block_id,
             kv_len=kv_len, is_full_block=is_full_block, is_stream=True,
             pre_cache_k=pre_cache_k, pre_cache_v=pre_cache_v, local_range=local_range)
-        if fa is not None:
-            x = gate_add(x, gate_msa, self_attn_output)
-        else:
-            x = self.gate(x, gate_msa, self_attn_output)
+        ca_out = None  # fast path: cross-attention output not yet added to x
         if fast:
             n3 = _unwrap(self.norm3)
             ca = self.cross_attn
             if token and type(getattr(ca, "q", None)) is FP8Linear and ca.q.mode == "token":
-                # norm3 also emits the per-token FP8 codes of its output: the cross-attention
-                # q projection takes them instead of quantising xn again
-                xn, x8, s8 = layer_norm(x, n3.weight, n3.bias, eps=getattr(n3, "eps", 1e-6),
-                                        emit_fp8=True)
+                # gate-add and norm3 in one pass; norm3 also emits the per-token FP8 codes of
+                # its output, which the cross-attention q projection takes directly (its bf16
+                # output only when the cross-attention would read it)
+                skip = _cross_fast_path(dit, ca, x)
+                x, xn, x8, s8 = gate_add_layer_norm(x, gate_msa, self_attn_output, n3.weight,
+                                                    n3.bias, eps=getattr(n3, "eps", 1e-6),
+                                                    emit_fp8=True, want_out=not skip)
+                xn = x if xn is None else xn
                 ca._fvb_x8 = (xn, x8, s8)
             else:
+                x = gate_add(x, gate_msa, self_attn_output)
                 xn = layer_norm(x, n3.weight, n3.bias, eps=getattr(n3, "eps", 1e-6))
-            x = fused_gate_add(x, None, ca(xn, context, is_stream=is_stream))
+            ca_out = ca(xn, context, is_stream=is_stream)
         else:
+            if fa is not None:
+                x = gate_add(x, gate_msa, self_attn_output)
+            else:
+                x = self.gate(x, gate_msa, self_attn_output)
             x = x + self.cross_attn(self.norm3(x), context, is_stream=is_stream)
         if fa is not None:
             ffn = self.ffn
-            if token and isinstance(ffn, FP8FFN) and ffn.lin0.mode == "token":
-                input_x, x8, s8 = fused_ln_modulate(x, scale_mlp, shift_mlp,
-                                                    eps=_module_eps(self.norm2), emit_fp8=True)
+            if ca_out is not None and token and isinstance(ffn, FP8FFN) \
+                    and ffn.lin0.mode == "token":
+                # cross-attention add and norm2 in one pass; the FFN reads only the FP8 codes
+                x, _, x8, s8 = gate_add_ln_modulate(x, None, ca_out, scale_mlp, shift_mlp,
+                                                    eps=_module_eps(self.norm2), emit_fp8=True,
+                                                    want_out=False)
                 y = ffn_fp8(x8.view(-1, x.shape[-1]), s8, ffn.lin0, ffn.lin2).view(x.shape)
             else:
+                if ca_out is not None:
+                    x = fused_gate_add(x, None, ca_out)
                 input_x = ln_mod(x, scale_mlp, shift_mlp, eps=_module_eps(self.norm2))
                 y = self.ffn(input_x)
             x = gate_add(x, gate_mlp, y)

@@ -141,7 +141,8 @@ FVB_API int fvb_rms_rope(const void* x, int64_t x_ld, const void* w, const float
  *   xn = bf16((x-mean)/sqrt(var+eps));  out = bf16(bf16(xn*bf16(1+scale)) + shift)
  * x/out [B,L,D] bf16, scale/shift [B,1,D] bf16 (note: scale BEFORE shift).
  * q8/q_scale (optional, both or neither): also emit the row's FP8 E4M3 codes with a
- * per-token scale exactly as fvb_quant_fp8(out, FVB_SCALE_ROW) would. */
+ * per-token scale exactly as fvb_quant_fp8(out, FVB_SCALE_ROW) would.  out may be NULL
+ * when q8 is given (a consumer that takes only the FP8 codes). */
 FVB_API int fvb_ln_modulate(const void* x, const void* scale, const void* shift, int64_t B, int64_t L,
                     int64_t D, float eps, void* out, void* q8, float* q_scale,
                     fvb_stream_t stream);
@@ -152,9 +153,25 @@ FVB_API int fvb_ln_modulate(const void* x, const void* scale, const void* shift,
  *   (w, b [D] bf16; either may be NULL).
  * q8/q_scale (optional, both or neither): also emit out's per-token FP8 E4M3 codes and scales
  * exactly as fvb_quant_fp8(out, FVB_SCALE_ROW) would (the cross-attention q projection's
- * input quantisation, fp8_linear.py:60-66, done in the same pass). */
+ * input quantisation, fp8_linear.py:60-66, done in the same pass).  out may be NULL when
+ * q8 is given. */
 FVB_API int fvb_layer_norm(const void* x, const void* w, const void* b, int64_t rows, int64_t D,
                    float eps, void* out, void* q8, float* q_scale, fvb_stream_t stream);
+
+/* The gated residual add fused into the norm that reads its result (the DiT block runs
+ * gate-add -> norm3 and cross-attention add -> norm2 back to back, wan_video_dit DiTBlock
+ * forward): x_out = fvb_gate_add(x, gate, r) (bitwise), then the norm of x_out exactly as
+ * fvb_ln_modulate / fvb_layer_norm compute it; the residual stream is read once.
+ * gate [B,1,D] or NULL (plain add); x_out must not alias x or r; out may be NULL when q8
+ * is given. */
+FVB_API int fvb_gate_add_ln_modulate(const void* x, const void* gate, const void* r, void* x_out,
+                                     const void* scale, const void* shift, int64_t B, int64_t L,
+                                     int64_t D, float eps, void* out, void* q8, float* q_scale,
+                                     fvb_stream_t stream);
+FVB_API int fvb_gate_add_layer_norm(const void* x, const void* gate, const void* r, void* x_out,
+                                    const void* w, const void* b, int64_t B, int64_t L, int64_t D,
+                                    float eps, void* out, void* q8, float* q_scale,
+                                    fvb_stream_t stream);
 
 /* ------------------------------------------------- a9: gated residual
  * Replaces fused_gate_add(x, gate, residual) (fused_adaln.py:74-85; kernel :45-57):

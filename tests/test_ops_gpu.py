@@ -60,6 +60,66 @@ def test_quantize_fp8_bitexact(M, K, mode):
     assert torch.equal(s.cpu(), sr.float())
 
 
+def _near_midpoint_rows(rows, K, seed):
+    """bf16 rows whose quotients x / s (s = row amax / 448, the reference's fp32 IEEE
+    divide) sit on or next to e4m3 rounding midpoints or in the e4m3 subnormal range.
+    Even rows: s with few mantissa bits, so x / s is exactly a midpoint m (a tie).  Odd
+    rows: an amax found by search for which some bf16 x round to a different e4m3 code
+    through x * fl(1/s) than through x / s; the row holds those x (both signs)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    mids = [(1 + (2 * i + 1) / 16) * 2.0 ** k for k in range(-6, 9) for i in range(8)]
+    mids = [m for m in mids if m < 448] + [(2 * i + 1) * 2.0 ** -10 for i in range(8)]
+    mids = np.array(mids + [1.0, 1.125, 2.0 ** -7, 448.0], np.float64)
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.int16)
+    allx = torch.from_numpy(bits).view(torch.bfloat16).float().numpy()
+    allx = allx[np.isfinite(allx)]
+
+    def codes(v):
+        return torch.from_numpy(np.clip(v, -448, 448).astype(np.float32)).to(
+            torch.float8_e4m3fn).view(torch.uint8).numpy()
+
+    out = np.zeros((rows, K), np.float32)
+    for r in range(rows):
+        if r % 2 == 0:
+            s = (1.0, 1.5, 1.25)[r // 2 % 3] * 2.0 ** int(rng.integers(-8, 2))
+            amax = 448 * s
+            pick = np.resize(mids * s * rng.choice([-1.0, 1.0], size=mids.size), K - 1)
+        else:
+            while True:
+                amax = float(torch.tensor(rng.uniform(0.01, 100)).to(torch.bfloat16).float())
+                sf = np.float32(amax) / np.float32(448.0)
+                xs = allx[np.abs(allx) <= amax]
+                diff = xs[codes(xs / sf) != codes(xs * (np.float32(1.0) / sf))]
+                if diff.size:
+                    break
+            pick = np.resize(np.concatenate([diff, -diff]), K - 1)
+        out[r, :K - 1] = pick
+        out[r, K - 1] = amax
+    x = torch.from_numpy(out).to(torch.bfloat16)
+    assert torch.equal(x.float(), torch.from_numpy(out))  # every value exact in bf16
+    return x
+
+
+def test_quantize_fp8_near_midpoints():
+    """Quotients next to e4m3 rounding midpoints and in the subnormal range: the codes must
+    still equal the reference's IEEE divide (token mode, row kernels and the FFN path's
+    quantisation with a given amax)."""
+    from flashvsr_sm89_ops_b200 import _lib, quantize_fp8
+    x = _near_midpoint_rows(16, 1536, 5)
+    q, s = quantize_fp8(x.to(DEV), "token")
+    qr, sr = O.quantize_fp8(x, "token")
+    assert torch.equal(q.view(torch.uint8).cpu(), qr.view(torch.uint8))
+    assert torch.equal(s.cpu(), sr.float())
+    xd = x.to(DEV)
+    amax = xd.float().abs().amax(dim=1).contiguous()
+    q2 = torch.empty_like(q)
+    s2 = torch.empty_like(s)
+    _lib.call("fvb_quant_fp8_with_amax", _lib.ptr(xd), x.shape[0], x.shape[1], _lib.ptr(amax),
+              _lib.FVB_SCALE_ROW, _lib.ptr(q2), _lib.ptr(s2), _lib.stream_of(xd))
+    assert torch.equal(q2.view(torch.uint8).cpu(), qr.view(torch.uint8))
+
+
 def test_quantize_fp8_tensor_ragged_and_empty():
     from flashvsr_sm89_ops_b200 import quantize_fp8
     x = torch.randn(7, 13, generator=gen(3)).to(torch.bfloat16)
@@ -139,6 +199,39 @@ def test_layer_norm_affine(L, D, with_bias):
     assert torch.equal(out2, out)
     qq, ss = quantize_fp8(out.reshape(-1, D), "token")
     assert torch.equal(q8.view(torch.uint8), qq.view(torch.uint8)) and torch.equal(qs, ss)
+
+
+@pytest.mark.parametrize("B,L,D,gated", [(1, 4224, 1536, True), (2, 37, 256, False)])
+def test_gate_add_fused_norms(B, L, D, gated):
+    """The gated residual add fused into LN-modulate / affine LayerNorm equals the two
+    separate kernels bit for bit (residual, bf16 output and FP8 codes), with and without
+    the bf16 output."""
+    from flashvsr_sm89_ops_b200.fused_adaln import (fused_gate_add, fused_ln_modulate,
+                                                    gate_add_layer_norm, gate_add_ln_modulate,
+                                                    layer_norm)
+    x = torch.randn(B, L, D, generator=gen(11)).to(torch.bfloat16).to(DEV)
+    r = torch.randn(B, L, D, generator=gen(12)).to(torch.bfloat16).to(DEV)
+    g = torch.randn(B, 1, D, generator=gen(13)).to(torch.bfloat16).to(DEV) if gated else None
+    mod = torch.randn(B, 2, D, generator=gen(14)).to(torch.bfloat16).to(DEV)
+    shift, scale = mod[:, 0:1].contiguous(), mod[:, 1:2].contiguous()
+    w = (1 + 0.1 * torch.randn(D, generator=gen(15))).to(torch.bfloat16).to(DEV)
+    b = (0.1 * torch.randn(D, generator=gen(16))).to(torch.bfloat16).to(DEV)
+    xs = fused_gate_add(x, g, r)
+    o1, q1, s1 = fused_ln_modulate(xs, scale, shift, emit_fp8=True)
+    xn, o, q, qs = gate_add_ln_modulate(x, g, r, scale, shift, emit_fp8=True)
+    assert torch.equal(xn, xs) and torch.equal(o, o1)
+    assert torch.equal(q.view(torch.uint8), q1.view(torch.uint8)) and torch.equal(qs, s1)
+    xn, o, q, qs = gate_add_ln_modulate(x, g, r, scale, shift, emit_fp8=True, want_out=False)
+    assert o is None and torch.equal(xn, xs)
+    assert torch.equal(q.view(torch.uint8), q1.view(torch.uint8)) and torch.equal(qs, s1)
+    o2, q2, s2 = layer_norm(xs, w, b, emit_fp8=True)
+    xn, o, q, qs = gate_add_layer_norm(x, g, r, w, b, emit_fp8=True)
+    assert torch.equal(xn, xs) and torch.equal(o, o2)
+    assert torch.equal(q.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(qs, s2)
+    xn, o, q, qs = gate_add_layer_norm(x, g, r, w, b, emit_fp8=True, want_out=False)
+    assert o is None and torch.equal(xn, xs) and torch.equal(q.view(torch.uint8), q2.view(torch.uint8))
+    xn, o = gate_add_layer_norm(x, g, r, w, None)
+    assert torch.equal(xn, xs) and torch.equal(o, layer_norm(xs, w, None))
 
 
 # ----------------------------------------------------------------------------- RMS+RoPE
