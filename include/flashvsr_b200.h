@@ -159,8 +159,8 @@ FVB_API int fvb_layer_norm(const void* x, const void* w, const void* b, int64_t 
                    float eps, void* out, void* q8, float* q_scale, fvb_stream_t stream);
 
 /* The gated residual add fused into the norm that reads its result (the DiT block runs
- * gate-add -> norm3 and cross-attention add -> norm2 back to back, wan_video_dit DiTBlock
- * forward): x_out = fvb_gate_add(x, gate, r) (bitwise), then the norm of x_out exactly as
+ * gate-add -> norm3 and cross-attention add -> norm2 back to back, integrate.py:167-173):
+ * x_out = fvb_gate_add(x, gate, r) (bitwise), then the norm of x_out exactly as
  * fvb_ln_modulate / fvb_layer_norm compute it; the residual stream is read once.
  * gate [B,1,D] or NULL (plain add); x_out must not alias x or r; out may be NULL when q8
  * is given. */
