@@ -428,7 +428,7 @@ def traffic_from_profiles(kernel):
 def run_b200(args, world, rank, local_rank):
     import torch.distributed as dist
     from flashvsr_sm89_ops_b200 import _lib
-    from flashvsr_sm89_ops_b200.runner import StreamingDiT
+    from flashvsr_sm89_ops_b200.runner import HostStream, StreamingDiT
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -482,22 +482,18 @@ def run_b200(args, world, rank, local_rank):
     ms_max = float(t.item())
     value = world * tokens * args.steps / (ms_max / 1e3)
 
-    # end to end through the public API: pinned host input -> step -> host output
+    # end to end through the public API: pinned host input -> step -> pinned host output for
+    # every step, the transfers overlapped with the neighbouring steps' compute (HostStream)
     x_host = torch.empty(x_static.shape, dtype=x_static.dtype, pin_memory=True)
     x_host.copy_(x_static.cpu())
-    y_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
-    for _ in range(2):
-        x_static.copy_(x_host, non_blocking=True)
-        step()
-        y_host.copy_(y, non_blocking=True)
+    y_hosts = [torch.empty(y.shape, dtype=y.dtype, pin_memory=True) for _ in range(2)]
+    hs = HostStream(step, x_static, y)
+    hs.run([x_host] * 2, y_hosts)
     torch.cuda.synchronize(dev)
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
-    for _ in range(args.steps):
-        x_static.copy_(x_host, non_blocking=True)
-        step()
-        y_host.copy_(y, non_blocking=True)
+    hs.run([x_host] * args.steps, [y_hosts[i & 1] for i in range(args.steps)])
     e3.record(stream)
     torch.cuda.synchronize(dev)
     barrier()

@@ -252,14 +252,15 @@ __global__ void __launch_bounds__(1024) draft_topk_kernel(const float* __restric
 //      copies, all in flight at once; a row pitch of d + 4 floats keeps the
 //      per-thread 16-byte reads conflict-free);
 //      thread (r, half) scores key row r against half of the group's queries;
-//   3. warp w selects for query w: scores become order-preserving integer keys, the
-//      nsel-th largest key is found bit by bit (32 warp-wide counts), and keys equal to
-//      it are taken in index order, so ties go to the lower key index;
+//   3. warp w selects for query w: scores become order-preserving integer keys (held in
+//      registers up to 256 past blocks), the nsel-th largest key is found bit by bit (32
+//      warp-wide counts), and keys equal to it are taken in index order, so ties go to
+//      the lower key index;
 //   4. the warp writes the query's keep row: own time row, selected past blocks, never
 //      a future row.
 // ---------------------------------------------------------------------------
 constexpr int kTopkThreads = 256;
-constexpr int kTopkQ = 8;    // query blocks per CTA (one selecting warp each)
+constexpr int kTopkQ = 4;    // query blocks per CTA (one selecting warp each)
 constexpr int kTopkKC = 128;  // key rows per shared-memory chunk
 
 __device__ __forceinline__ uint32_t ordered_key(float s) {
@@ -332,13 +333,27 @@ __global__ void __launch_bounds__(kTopkThreads) causal_topk_kernel(
   const int npast = qrow * per_row;
   const int nsel = (int)floorf(ratio * (float)npast);
   const uint32_t* kq = key + w * NK;
-  // largest T with #{key >= T} >= nsel, i.e. the nsel-th largest key
+  // largest T with #{key >= T} >= nsel, i.e. the nsel-th largest key; up to 256 past
+  // blocks the keys stay in registers (8 per lane), beyond that they are re-read
   uint32_t T = 0;
+  constexpr int kRegKeys = 8;
+  uint32_t kr[kRegKeys];
+#pragma unroll
+  for (int t = 0; t < kRegKeys; ++t) {
+    const int i = lane + 32 * t;
+    kr[t] = i < npast ? kq[i] : 0u;  // 0 is below every key of a finite score
+  }
+  const bool in_regs = npast <= 32 * kRegKeys;
   if (nsel > 0) {
     for (int b = 31; b >= 0; --b) {
       const uint32_t cand = T | (1u << b);
       int c = 0;
-      for (int i = lane; i < npast; i += 32) c += kq[i] >= cand;
+      if (in_regs) {
+#pragma unroll
+        for (int t = 0; t < kRegKeys; ++t) c += kr[t] >= cand;
+      } else {
+        for (int i = lane; i < npast; i += 32) c += kq[i] >= cand;
+      }
       if ((int)__reduce_add_sync(0xffffffffu, (unsigned)c) >= nsel) T = cand;
     }
   }

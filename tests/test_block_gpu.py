@@ -177,6 +177,27 @@ def test_streaming_runner_graph_replay_equals_eager():
     assert _lib.device_error() == 0
 
 
+def test_host_stream_overlapped_copies_equal_plain_steps():
+    """HostStream (uploads and downloads on a copy stream, overlapped with the steps) gives
+    every step's output exactly as a plain copy-in / step / copy-out sequence does."""
+    from flashvsr_sm89_ops_b200.runner import HostStream, StreamingDiT
+    r = StreamingDiT(num_layers=2, height=256, width=384, device=DEV)
+    r.prime()
+    x = r.make_input(2)
+    g, y = r.capture(x)
+    xs = [r.make_input(2, seed=20 + i).cpu().pin_memory() for i in range(5)]
+    ref = []
+    for xh in xs:
+        x.copy_(xh)
+        g.replay()
+        ref.append(y.cpu())
+    outs = [torch.empty(y.shape, dtype=y.dtype, pin_memory=True) for _ in xs]
+    HostStream(g.replay, x, y).run(xs, outs)
+    torch.cuda.synchronize()
+    for o, e in zip(outs, ref):
+        assert torch.equal(o, e)
+
+
 def test_compat_stub_call_shape():
     """block_sparse_attn_func with the mit-han-lab signature (compat_bsa.py:31-67)."""
     import flashvsr_sm89_ops_b200  # noqa: F401  (installs the stand-in)
