@@ -87,3 +87,44 @@ def test_forward_refuses_cpu(monkeypatch):
     fl = FP8Linear(lin)
     with pytest.raises(ValueError, match="CUDA"):
         fl(torch.zeros(2, 32, dtype=torch.bfloat16))
+
+
+def test_kv_arena_reuses_only_unheld_windows():
+    """The streaming KV arena (host-side bookkeeping, CPU tensors here): a new row goes right
+    after the given cache when no live handed-out cache covers those windows; otherwise the
+    cache is copied into a fresh arena, so a cache a caller still holds never changes."""
+    import gc
+
+    from flashvsr_sm89_ops_b200.integrate import _arena_slot
+    D, row = 8, 2  # 8 channels, 2 windows per time row
+    cpu = torch.device("cpu")
+    ar, a, b = _arena_slot(None, 6, row, D, cpu)  # start chunk: 3 rows, no cache
+    assert (a, b) == (0, 0) and ar.cap == 6 + 4 * row
+    ar.rows(0, 6).copy_(torch.arange(6 * 128 * D, dtype=torch.float32).view(-1, D))
+    c0 = ar.hand_out(0, 6)
+    # a step given c0 appends in place after it
+    ar1, a1, b1 = _arena_slot(c0, row, row, D, cpu)
+    assert ar1 is ar and (a1, b1) == (0, 6)
+    c1 = ar.hand_out(2, 8)  # the step's returned cache (oldest row dropped)
+    # c1 is alive and covers windows [6, 8): the same step given c0 again must not reuse them
+    ar2, a2, b2 = _arena_slot(c0, row, row, D, cpu)
+    assert ar2 is not ar and (a2, b2) == (0, 6)
+    assert torch.equal(ar2.rows(0, 6), c0.reshape(-1, D))
+    # once c1 is gone the windows are free again
+    del c1
+    gc.collect()
+    ar3, a3, b3 = _arena_slot(c0, row, row, D, cpu)
+    assert ar3 is ar and (a3, b3) == (0, 6)
+    # a real stream (each step gets the previous step's cache): 4 in-place appends fill the
+    # 4 spare rows, the 5th step copies the cache into a new arena
+    c, arenas = c0, []
+    for _ in range(5):
+        arx, ax, bx = _arena_slot(c, row, row, D, cpu)
+        arenas.append(arx)
+        c = arx.hand_out(ax + row, bx + row)
+        assert c.shape[0] == 6  # always 3 time rows of 2 windows
+    assert all(x is ar for x in arenas[:4]) and arenas[4] is not ar
+    # a tensor that did not come from an arena is copied
+    plain = torch.zeros(6, 128, D)
+    arp, ap, bp = _arena_slot(plain, row, row, D, cpu)
+    assert (ap, bp) == (0, 6) and torch.equal(arp.rows(0, 6), plain.reshape(-1, D))
