@@ -419,7 +419,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int col_q = h * kTile;
-  const int jmax = it[0].cnt > it[1].cnt ? it[0].cnt : it[1].cnt;
 
   if (warp == 8 || warp == 9) {
     // ------------------------------------------------------------ TMA producer of item x
