@@ -198,7 +198,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     bool ok = true;
     for (int j = 0; j < cnt; ++j) {
       const uint32_t ph = (uint32_t)j & 1u;
-      if (!mbar_wait(s_full, ph, 0x308u)) {
+      // every branch around a tcgen05.ld / st below is warp-uniform (they are .sync.aligned)
+      if (!__all_sync(0xffffffffu, mbar_wait(s_full, ph, 0x308u))) {
         ok = false;
         break;
       }
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       float* xm = xmax + (j & 1) * 256;
       xm[g * 128 + row] = pm;
       mbar_arrive(&x_bar[j & 1]);
-      if (!mbar_wait(&x_bar[j & 1], (uint32_t)(j >> 1) & 1u, 0x309u)) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&x_bar[j & 1], (uint32_t)(j >> 1) & 1u, 0x309u))) {
         ok = false;
         break;
       }
@@ -252,7 +253,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       l = l * alpha + (la + lb);
       // P_j of this half into the first 32 columns of its own 64-column S range
       tmem_st_32x32b_x32(tS + lane_addr + (uint32_t)(g * 64), pk);
-      if (raise && j > 0) {  // rescale O in place; every earlier MMA is complete (S_j commit)
+      // rescale O in place (every earlier MMA is complete: S_j commit) when any row of the
+      // warp raised its max; the other rows have alpha = 1 and keep their values exactly
+      if (__any_sync(0xffffffffu, raise) && j > 0) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           uint32_t o[32];
@@ -280,6 +283,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         have_o = true;
       }
     }
+    have_o = __all_sync(0xffffffffu, have_o);  // the tcgen05.ld below runs warp-wide or not
     const float inv = lt > 0.f ? 1.0f / lt : 0.f;
     const int qrow = qb * kTile + row;
     const int64_t orow =
@@ -573,11 +577,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < 4; ++t) mx[t] = fmaxf(mx[t], __uint_as_float(s[124 + t]));
       const float mb = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * c;  // log2 domain
       float alpha = 1.f;
-      const bool rescale = mb > m_used + kLazy;
-      if (rescale) {
+      const bool raise = mb > m_used + kLazy;
+      if (raise) {
         alpha = (m_used == -INFINITY) ? 0.f : ex2_approx(m_used - mb);
         m_used = mb;
       }
+      // O is rescaled by the whole warp when any of its rows raised its max (tcgen05.ld / st
+      // are .sync.aligned); the other rows have alpha = 1 and keep their values exactly
+      const bool rescale = __any_sync(0xffffffffu, raise);
       const float msub = (m_used == -INFINITY) ? 0.f : m_used;
       const uint64_t cc = f2_pack(c, c);
       const uint64_t nm = f2_pack(-msub, -msub);
@@ -621,20 +628,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (have_o) tc_fence_after();
     const float inv = (have_o && l > 0.f) ? 1.0f / l : 0.f;
     if (me.qb >= 0) {
+      // rows past Lq (a partial last window) still take part in the warp-wide TMEM loads;
+      // only their stores are skipped
       const int qrow = me.qb * kTile + row;
-      if (qrow < args.Lq) {
-        const int64_t orow = args.row_map ? (int64_t)__ldg(args.row_map + qrow) : (int64_t)qrow;
-        uint4* dst = reinterpret_cast<uint4*>(args.out + orow * args.ldo + col_q);
+      const bool row_ok = qrow < args.Lq;
+      const int64_t orow =
+          args.row_map ? (int64_t)__ldg(args.row_map + (row_ok ? qrow : 0)) : (int64_t)qrow;
+      uint4* dst = reinterpret_cast<uint4*>(args.out + orow * args.ldo + col_q);
 #pragma unroll 1
-        for (int hh = 0; hh < 4; ++hh) {
-          uint32_t o[32];
-          if (have_o) {
-            tmem_ld_32x32b_x32(tO + (uint32_t)(hh * 32), o);
-            tmem_ld_wait();
-          } else {
+      for (int hh = 0; hh < 4; ++hh) {
+        uint32_t o[32];
+        if (have_o) {
+          tmem_ld_32x32b_x32(tO + (uint32_t)(hh * 32), o);
+          tmem_ld_wait();
+        } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = 0u;
-          }
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        if (row_ok) {
 #pragma unroll
           for (int cch = 0; cch < 4; ++cch) {
             float f[8];
