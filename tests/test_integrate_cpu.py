@@ -128,3 +128,21 @@ def test_kv_arena_reuses_only_unheld_windows():
     plain = torch.zeros(6, 128, D)
     arp, ap, bp = _arena_slot(plain, row, row, D, cpu)
     assert (ap, bp) == (0, 6) and torch.equal(arp.rows(0, 6), plain.reshape(-1, D))
+
+
+def test_new_entry_points_refuse_cpu_tensors():
+    """The fused gated norms, block pooling and the pooled keep rule follow the pack's
+    contract for CPU tensors: ValueError naming CUDA, before any library call."""
+    from flashvsr_sm89_ops_b200 import lcsa
+    from flashvsr_sm89_ops_b200.fused_adaln import gate_add_layer_norm, gate_add_ln_modulate
+    x = torch.zeros(1, 128, 64, dtype=torch.bfloat16)
+    v = torch.zeros(1, 1, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        gate_add_ln_modulate(x, v, x, v, v, emit_fp8=True)
+    with pytest.raises(ValueError, match="CUDA"):
+        gate_add_layer_norm(x, v, x, None, None)
+    with pytest.raises(ValueError, match="CUDA"):
+        lcsa.block_mean_pool(x.view(128, 64))
+    with pytest.raises(ValueError, match="CUDA"):
+        lcsa.causal_topk_mask(x.view(128, 64), x.view(128, 64), 1, 1, k_pool_prefix=None,
+                              return_k_pool=True)
