@@ -28,8 +28,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("FVB_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("FVB_REFERENCE"),
+                    help="checkout of the reference package (or set FVB_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <path to the reference checkout> or set FVB_REFERENCE")
     sys.path.insert(0, args.reference)
     from flashvsr_sm89_ops import fp8_linear as R_lin
     from flashvsr_sm89_ops import tiling as R_til
