@@ -510,7 +510,11 @@ def run_b200(args, world, rank, local_rank):
     tiled = None
     if os.environ.get("FVB_SKIP_TILED") != "1":
         import torch.distributed as dist_mod
-        tiled = tiled_4k(runner, world, rank, dev, dist_mod)
+        try:  # the secondary 4K workload must not cost the step's line
+            tiled = tiled_4k(runner, world, rank, dev, dist_mod)
+        except Exception as e:  # noqa: BLE001
+            tiled = {"error": f"{type(e).__name__}: {e}"[:300]}
+            print(f"tiled_4k failed: {tiled['error']}", file=sys.stderr, flush=True)
     devs = _lib.device_error()
     if devs:
         raise RuntimeError(f"device error word set: {devs:#x}")
