@@ -39,9 +39,10 @@ def _b200_block_sparse_attn_func(
     """
     if streaming_info is not None or is_causal or dropout_p != 0.0 or return_attn_probs:
         raise NotImplementedError(
-            "flashvsr-sm89-ops-b200 LCSA covers the FlashVSR call shape only "
-            "(dense-per-batch, no dropout, no causal, no attn-probs). "
-            "Install the real block_sparse_attn package for other shapes.")
+            "block_sparse_attn_func stand-in (B200 pack): this call asks for streaming_info, "
+            "is_causal, dropout or returned probabilities, which the tcgen05 kernel does not "
+            "implement; it serves FlashVSR's one call shape (batch 1, a block keep mask). Use "
+            "the mit-han-lab block_sparse_attn package for other modes.")
     from .lcsa import block_sparse_attention
 
     sq, heads, dim = q.shape

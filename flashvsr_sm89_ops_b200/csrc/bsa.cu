@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* pv_done = bars + 7;
   uint64_t* x_bar = bars + 8;  // [2]
   uint64_t* l_bar = bars + 10;
+  uint64_t* drain = bars + 11;  // MMA unwind: completion of every MMA this CTA issued
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   float* xmax = reinterpret_cast<float*>(bars + 16);  // [2 parity][2 halves][128]
   float* xl = xmax + 2 * 2 * 128;                     // [2 halves][128]
@@ -112,6 +113,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(&x_bar[0], kSoftmaxThreads);
     mbar_init(&x_bar[1], kSoftmaxThreads);
     mbar_init(l_bar, kSoftmaxThreads);
+    mbar_init(drain, 1);
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -135,6 +137,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive_expect_tx(q_full, kTileBytes);
       tma_load_2d(sQ, &tmQ, q_full, col_q, qb * kTile);
       tma_load_2d(sQ + kAtom, &tmQ, q_full, col_q + 64, qb * kTile);
+      int nk = 0, nv = 0;  // K / V tiles issued (each slot holds the newest one)
       for (int j = 0; j < cnt; ++j) {
         const uint32_t ph = (uint32_t)j & 1u;
         const int krow = __ldg(sel + j) * kTile;
@@ -142,11 +145,18 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_arrive_expect_tx(k_full, kTileBytes);
         tma_load_2d(sK, &tmK, k_full, col_q, krow);
         tma_load_2d(sK + kAtom, &tmK, k_full, col_q + 64, krow);
+        ++nk;
         if (!mbar_wait(v_empty, ph ^ 1u, 0x302u)) break;
         mbar_arrive_expect_tx(v_full, kTileBytes);
         tma_load_2d(sV, &tmV, v_full, col_q, krow);
         tma_load_2d(sV + kAtom, &tmV, v_full, col_q + 64, krow);
+        ++nv;
       }
+      // Drain: no tile load may still be writing shared memory when the CTA exits
+      // (complete already on the normal path; bounded waits after a timeout).
+      mbar_wait(q_full, 0, 0x30Cu);
+      if (nk) mbar_wait(k_full, (uint32_t)(nk - 1) & 1u, 0x30Cu);
+      if (nv) mbar_wait(v_full, (uint32_t)(nv - 1) & 1u, 0x30Cu);
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
@@ -185,6 +195,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc_commit(pv_done);
         tc_commit(v_empty);
       }
+      // Drain: every MMA issued above completes before TMEM is freed.
+      tc_commit(drain);
+      mbar_wait(drain, 0, 0x30Du);
     }
   } else {
     // ------------------------------------------------------------ softmax warps
@@ -382,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sK[2] = {base + kTileBytes, base + 4 * kTileBytes};
   uint8_t* sV[2] = {base + 2 * kTileBytes, base + 5 * kTileBytes};
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + 6 * kTileBytes);
-  enum { Q_FULL = 0, K_FULL, K_EMPTY, V_FULL, V_EMPTY, S_FULL, S_FREE, P_FULL, PV_DONE, kNB };
+  enum { Q_FULL = 0, K_FULL, K_EMPTY, V_FULL, V_EMPTY, S_FULL, S_FREE, P_FULL, PV_DONE, DRAIN, kNB };
   auto BAR = [&](int x, int i) { return bars + x * kNB + i; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kNB);
 
@@ -436,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
       bool ok = true;
+      int nk = 0, nv = 0;  // K / V tiles issued (each slot holds the newest one)
       mbar_arrive_expect_tx(BAR(x, Q_FULL), kTileBytes);
       tma_load_2d(q_s, &tmQ, BAR(x, Q_FULL), col_q, me.qb * kTile);
       tma_load_2d(q_s + kAtom, &tmQ, BAR(x, Q_FULL), col_q + 64, me.qb * kTile);
@@ -448,6 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(BAR(x, K_FULL), kTileBytes);
           tma_load_2d(k_s, &tmK, BAR(x, K_FULL), col_q, krow);
           tma_load_2d(k_s + kAtom, &tmK, BAR(x, K_FULL), col_q + 64, krow);
+          ++nk;
         }
         if (j >= 1) {
           const int jv = j - 1;
@@ -456,8 +471,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(BAR(x, V_FULL), kTileBytes);
           tma_load_2d(v_s, &tmV, BAR(x, V_FULL), col_q, vrow);
           tma_load_2d(v_s + kAtom, &tmV, BAR(x, V_FULL), col_q + 64, vrow);
+          ++nv;
         }
       }
+      // Drain: no tile load may still be writing shared memory when the CTA exits
+      // (complete already on the normal path; bounded waits after a timeout).
+      mbar_wait(BAR(x, Q_FULL), 0, 0x70Bu);
+      if (nk) mbar_wait(BAR(x, K_FULL), (uint32_t)(nk - 1) & 1u, 0x70Bu);
+      if (nv) mbar_wait(BAR(x, V_FULL), (uint32_t)(nv - 1) & 1u, 0x70Bu);
     }
   } else if (warp == 10 || warp == 11) {
     // ------------------------------------------------------------ MMA issuer of item x
@@ -526,6 +547,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         issue_pv(j);
         issue_s(j + 2);
       }
+      // Drain: every MMA issued above completes before TMEM is freed.
+      tc_commit(BAR(x, DRAIN));
+      mbar_wait(BAR(x, DRAIN), 0, 0x70Cu);
     }
   } else {
     // ------------------------------------------------------------ softmax warpgroups

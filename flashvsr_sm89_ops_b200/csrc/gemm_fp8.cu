@@ -103,7 +103,8 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* drain = tempty + 2;  // MMA unwind: completion of every MMA this CTA issued
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = warp_id_uniform();
   const int lane = threadIdx.x & 31;
@@ -121,6 +122,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], EPI_WARPS);
     }
+    mbar_init(drain, 1);
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -141,6 +143,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      int64_t issued = 0;  // loads issued so far; load i fills stage i % STAGES
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * BM;
         const int n0 = (tile % n_tiles) * BN;
@@ -152,12 +155,18 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], (uint32_t)((BM + BN) * BK));
           tma_load_2d(sA + stage * BM * BK, &tmA, &full[stage], kb * BK, m0);
           tma_load_2d(sB + stage * BN * BK, &tmB, &full[stage], kb * BK, n0);
+          ++issued;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
+      // Drain: no load of this CTA may still be writing its shared memory when the CTA
+      // exits.  The last STAGES loads are the newest phase of their stages' full barriers
+      // (already complete on the normal path; bounded waits after a timeout).
+      for (int64_t i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i)
+        mbar_wait(&full[i % STAGES], (uint32_t)((i / STAGES) & 1), 0x10Au);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -167,6 +176,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
       uint32_t phase = 0;
       int t = 0;
       bool ok = true;
+      bool any = false;  // whether this thread issued an MMA
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
         const int buf = t & 1;
         const uint32_t tph = (uint32_t)(t >> 1) & 1u;
@@ -187,6 +197,7 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
             const uint64_t db = smem_desc_sw128(b0 + k * 32, 16, 1024);
             mma_f8f6f4(d_tmem, da, db, idesc, (kb | k) != 0 ? 1u : 0u);
           }
+          any = true;
           tc_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -194,6 +205,12 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
           }
         }
         if (ok) tc_commit(&tfull[buf]);
+      }
+      // Drain: every MMA issued above completes before TMEM is freed (on the normal path
+      // the epilogue has already waited for all of them).
+      if (any) {
+        tc_commit(drain);
+        mbar_wait(drain, 0, 0x10Bu);
       }
     }
   } else {
@@ -218,7 +235,9 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
       const uint32_t tph = (uint32_t)(t >> 1) & 1u;
       const int m0 = (tile / n_tiles) * BM;
       const int n0 = (tile % n_tiles) * BN;
-      if (!mbar_wait(&tfull[buf], tph, 0x104u)) break;
+      // warp-uniform: the tcgen05.ld below is .sync.aligned, so either every lane of the
+      // warp goes on or none does
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], tph, 0x104u))) break;
       tc_fence_after();
       const int rloc = q * 32 + lane;  // row within the tile == TMEM lane
       const int row = m0 + rloc;

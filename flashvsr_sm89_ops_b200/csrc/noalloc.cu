@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(256) quant_from_partials_kernel(
   }
   __syncthreads();
   const float amax = amax_s;
-  // s = max(amax, 1e-12) / 448, q = e4m3(clamp(x / s)), IEEE divides (fp8_quant.py:25-35)
+  // s = max(amax, 1e-12) / 448, q = e4m3(clamp(x / s)), IEEE divides (fp8_quant.py:25-35);
+  // the saturating conversion is the clamp and, like clamp-then-cast, keeps a NaN a NaN
   const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
   if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = __fdiv_rn(amax, 448.0f);
   const int64_t nvec = n >> 3;
@@ -88,14 +89,14 @@ __global__ void __launch_bounds__(256) quant_from_partials_kernel(
     for (int h = 0; h < 2; ++h) {
       float a[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = fminf(fmaxf(__fdiv_rn(f[4 * h + i], s), -448.f), 448.f);
+      for (int i = 0; i < 4; ++i) a[i] = __fdiv_rn(f[4 * h + i], s);
       w[h] = (uint32_t)f32x2_to_e4m3x2(a[0], a[1]) | ((uint32_t)f32x2_to_e4m3x2(a[2], a[3]) << 16);
     }
     qv[v] = make_uint2(w[0], w[1]);
   }
   if (blockIdx.x == 0) {
     for (int64_t i = nvec * 8 + threadIdx.x; i < n; i += blockDim.x)
-      q[i] = f32_to_e4m3(fminf(fmaxf(__fdiv_rn(__bfloat162float(x[i]), s), -448.f), 448.f));
+      q[i] = f32_to_e4m3(__fdiv_rn(__bfloat162float(x[i]), s));
   }
 }
 
@@ -138,8 +139,13 @@ extern "C" int fvb_quant_fp8_tensor_noalloc(const void* x, int64_t M, int64_t K,
   using namespace fvb;
   cudaStream_t st = (cudaStream_t)stream;
   FVB_REQUIRE(M >= 0 && K >= 0, "fvb_quant_fp8_tensor_noalloc: negative size");
-  const int64_t n = M * K;
   const int64_t max_n = (int64_t)noalloc::kMaxPartials * noalloc::kChunk;
+  // reject before forming M * K, which could overflow int64 for huge sizes
+  FVB_REQUIRE(K == 0 || M <= max_n / K,
+              "fvb_quant_fp8_tensor_noalloc: %lld x %lld elements exceed the fixed scratch "
+              "limit of %lld; use fvb_quant_fp8 with a workspace",
+              (long long)M, (long long)K, (long long)max_n);
+  const int64_t n = M * K;
   FVB_REQUIRE(n <= max_n,
               "fvb_quant_fp8_tensor_noalloc: %lld elements exceed the fixed scratch limit of "
               "%lld (%d partials x %lld elements); use fvb_quant_fp8 with a workspace",

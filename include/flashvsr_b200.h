@@ -7,9 +7,11 @@
  *   FVB_ERR_UNSUPPORTED (a mode this pack does not implement),
  *   FVB_ERR_CUDA (a CUDA launch or runtime call failed).
  * fvb_last_error() returns the message of the last failure on the calling
- * thread.  No entry point synchronises the stream, allocates device memory or
- * keeps state between calls except the per-device error word read by
- * fvb_device_error().  Callers own every buffer; inputs are never written.
+ * thread.  No entry point synchronises the stream or allocates device memory.
+ * Device state kept between calls: the per-device error word read by
+ * fvb_device_error(), and the fixed scratch array of fvb_quant_fp8_tensor_noalloc
+ * (whose overlapping calls race; see its comment).  Callers own every buffer;
+ * inputs are never written.
  *
  * Tensor conventions: bf16 = IEEE bfloat16, fp8 = OCP FP8 E4M3 ("e4m3fn",
  * max 448, no infinities), all matrices row-major and contiguous.

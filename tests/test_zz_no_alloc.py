@@ -49,13 +49,17 @@ def test_noalloc_matches_regular_entry_point_twice():
     big[torch.rand(big.shape, generator=g) < 0.01] *= 20
     small = (torch.randn(333, 1000, generator=g) * 0.5).to(torch.bfloat16)  # ragged: 333000 % 8 == 0
     tail = torch.randn(7, 13, generator=g).to(torch.bfloat16)               # n % 8 != 0
-    for x in (big.to(torch.bfloat16), small, tail):
+    nan = torch.randn(2555, generator=g).to(torch.bfloat16)  # 2555 % 8 == 3
+    nan[123] = float("nan")   # a NaN stays NaN (clamp-then-cast keeps it): vector part
+    nan[2553] = float("nan")  # ... and in the scalar tail
+    nan = nan.reshape(511, 5)
+    for x in (big.to(torch.bfloat16), small, tail, nan):
         xd = x.to(dev)
         qr, sr = _regular(lib, xd, stream)
         qn, sn = _noalloc(lib, xd, stream)
         torch.cuda.synchronize(dev)
         assert torch.equal(qn.view(torch.uint8), qr.view(torch.uint8))
-        assert torch.equal(sn, sr)
+        assert torch.equal(sn, sr) or (torch.isnan(sn).all() and torch.isnan(sr).all())
     assert _lib.device_error() == 0
 
 
@@ -69,6 +73,10 @@ def test_noalloc_rejects_oversize_and_handles_empty():
     rc = lib.fvb_quant_fp8_tensor_noalloc(None, 1 << 20, 1 << 11, None, s.data_ptr(), stream)
     assert rc == _lib.FVB_ERR_INVALID
     assert b"scratch limit" in lib.fvb_last_error()
+    # 2^32 x 2^32 would overflow int64 if multiplied before the check
+    rc = lib.fvb_quant_fp8_tensor_noalloc(None, 1 << 32, 1 << 32, None, s.data_ptr(), stream)
+    assert rc == _lib.FVB_ERR_INVALID
+    assert b"scratch" in lib.fvb_last_error()
     rc = lib.fvb_quant_fp8_tensor_noalloc(None, 0, 1536, None, s.data_ptr(), stream)
     assert rc == _lib.FVB_OK
     torch.cuda.synchronize(dev)
