@@ -79,6 +79,8 @@ __global__ void __launch_bounds__(256) mask_to_csr_kernel(const uint8_t* __restr
 // grid (windows, ceil(C / 512)), 256 threads: threadIdx.x % 64 picks one 8-channel vector of
 // this CTA's 512-channel slice, threadIdx.x / 64 one of 4 token groups (32 tokens each, 8
 // loads in flight per thread); the 4 partial sums meet in shared memory in a fixed order.
+// The order is part of the keep rules' definition (the oracle restates it): partial g sums
+// tokens g, g+4, ..., g+124 in that order; mean = ((p0 + p1) + (p2 + p3)) / 128.
 __global__ void __launch_bounds__(256) pool_kernel(const __nv_bfloat16* __restrict__ x,
                                                     int64_t nblk, int64_t C, int round_bf16,
                                                     float* __restrict__ avg) {
@@ -116,32 +118,37 @@ __global__ void __launch_bounds__(256) pool_kernel(const __nv_bfloat16* __restri
 // a13 step 2: per (head, query block) scores over all key blocks, local mask,
 // softmax -> probabilities (bf16-rounded like the bf16 reference tensors).
 // grid (NQ, H), block 256; dynamic smem NK floats.
+// Every fp32 step has one fixed evaluation order, which the oracle restates
+// operation for operation, so the keep mask is bit-identical to it:
+//   score  = bf16(bf16(sum_e q[e] k[e]) / sqrt(d)), the sum sequential over e (the
+//            products of bf16 means are exact in fp32);
+//   e_j    = fp32(exp(double(score_j - max)))  (a double exp, so both sides round the
+//            same value to fp32);
+//   total  = sequential fp32 sum of e_j over j = 0..NK-1;
+//   prob_j = bf16(e_j / total).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) draft_scores_kernel(
     const float* __restrict__ aq, const float* __restrict__ ak, int64_t NQ, int64_t NK, int H,
     int d, const uint8_t* __restrict__ local, int64_t sq, int64_t sk, float* __restrict__ prob) {
   extern __shared__ float sc[];
   __shared__ float red[32];
+  __shared__ float qsh[256];
   const int64_t qi = blockIdx.x;
   const int h = blockIdx.y;
   const int64_t C = (int64_t)H * d;
   const float* qv = aq + qi * C + (int64_t)h * d;
-  const float inv_sqrt_d = 1.0f / sqrtf((float)d);  // python float 1/sqrt(D) in the reference
-  const float sqrt_d = sqrtf((float)d);
-  (void)inv_sqrt_d;
+  const float sqrt_d = sqrtf((float)d);  // python float math.sqrt(D), used in fp32
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  // one warp per key block: dot product over d
-  for (int64_t kj = wid; kj < NK; kj += nw) {
+  for (int e = threadIdx.x; e < d; e += blockDim.x) qsh[e] = qv[e];
+  __syncthreads();
+  // one thread per key block: the dot product in ascending e
+  for (int64_t kj = threadIdx.x; kj < NK; kj += blockDim.x) {
     const float* kv = ak + kj * C + (int64_t)h * d;
     float acc = 0.f;
-    for (int e = lane; e < d; e += 32) acc = __fmaf_rn(qv[e], kv[e], acc);
-    acc = warp_sum(acc);
-    if (lane == 0) {
-      // einsum output is bf16, then "/ math.sqrt(D)" -> bf16
-      float s = bf16r(__fdiv_rn(bf16r(acc), sqrt_d));
-      const bool on = local[(qi % sq) * sk + (kj % sk)] != 0;
-      sc[kj] = on ? s : -INFINITY;
-    }
+    for (int e = 0; e < d; ++e) acc = __fadd_rn(acc, __fmul_rn(qsh[e], __ldg(kv + e)));
+    const float s = bf16r(__fdiv_rn(bf16r(acc), sqrt_d));
+    const bool on = local[(qi % sq) * sk + (kj % sk)] != 0;
+    sc[kj] = on ? s : -INFINITY;
   }
   __syncthreads();
   float m = -INFINITY;
@@ -157,19 +164,13 @@ __global__ void __launch_bounds__(256) draft_scores_kernel(
   __syncthreads();
   m = red[0];
   __syncthreads();
-  float s = 0.f;
-  for (int64_t kj = threadIdx.x; kj < NK; kj += blockDim.x) {
-    float e = (sc[kj] == -INFINITY) ? 0.f : expf(sc[kj] - m);
-    sc[kj] = e;
-    s += e;
-  }
-  s = warp_sum(s);
-  if (lane == 0) red[wid] = s;
+  for (int64_t kj = threadIdx.x; kj < NK; kj += blockDim.x)
+    sc[kj] = (sc[kj] == -INFINITY) ? 0.f : (float)exp((double)__fsub_rn(sc[kj], m));
   __syncthreads();
-  if (wid == 0) {
-    float t = lane < nw ? red[lane] : 0.f;
-    t = warp_sum(t);
-    if (lane == 0) red[0] = t;
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int64_t kj = 0; kj < NK; ++kj) tot = __fadd_rn(tot, sc[kj]);
+    red[0] = tot;
   }
   __syncthreads();
   const float tot = red[0];
@@ -310,11 +311,13 @@ __global__ void __launch_bounds__(kTopkThreads) causal_topk_kernel(
         const float4 kk = kr[e];
 #pragma unroll
         for (int j = 0; j < kTopkQ / 2; ++j) {
+          // ascending e, each product and sum rounded on its own (no FMA contraction):
+          // the rule's defined evaluation order, restated exactly by the oracle
           const float4 qv = qs4[(half + 2 * j) * d4 + e];  // same address across the warp
-          acc[j] = __fmaf_rn(qv.x, kk.x, acc[j]);
-          acc[j] = __fmaf_rn(qv.y, kk.y, acc[j]);
-          acc[j] = __fmaf_rn(qv.z, kk.z, acc[j]);
-          acc[j] = __fmaf_rn(qv.w, kk.w, acc[j]);
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(qv.x, kk.x));
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(qv.y, kk.y));
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(qv.z, kk.z));
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(qv.w, kk.w));
         }
       }
 #pragma unroll
@@ -455,6 +458,7 @@ int fvb_draft_block_mask(const void* q_w, const void* k_w, int64_t H, int64_t NQ
   FVB_REQUIRE(q_w && k_w && local && keep && workspace, "fvb_draft_block_mask: NULL pointer");
   FVB_REQUIRE(aligned16(q_w) && aligned16(k_w), "fvb_draft_block_mask: alignment");
   FVB_REQUIRE(NK * 4 <= 200 * 1024, "fvb_draft_block_mask: NK too large");
+  FVB_REQUIRE(d <= 256, "fvb_draft_block_mask: head_dim %lld > 256", (long long)d);
   const int64_t C = H * d;
   float* aq = static_cast<float*>(workspace);
   float* ak = aq + NQ * C;

@@ -37,6 +37,7 @@ class StreamingDiT:
         g = torch.Generator(device=self.device).manual_seed(seed + 1)
         ctx = torch.randn(1, ctx_len, dim, generator=g, device=self.device).to(torch.bfloat16)
         dit.init_cross_kv(ctx)
+        self.ctx = ctx
         self.t_mod = torch.randn(1, 6, dim, generator=g, device=self.device).to(torch.bfloat16)
         self.caches = None
         self.graph = None

@@ -1,6 +1,7 @@
 """CPU restatement of the reference operator formulas (test infrastructure only).
 
-All functions take and return CPU tensors.  bf16 rounding points are placed
+Functions compute on the device of their inputs (CPU in the parity tests; the largest
+block-level checks evaluate the same code on the GPU in fp32).  bf16 rounding points are placed
 exactly where the reference kernels place them.  Citations are paths inside
 aireet/flashvsr-sm89-ops.
 """
@@ -27,11 +28,11 @@ def quantize_fp8(x2: torch.Tensor, mode: str = "tensor"):
     xf = x2.float()
     if mode == "tensor":
         if xf.numel() == 0:
-            return x2.to(E4M3), torch.zeros(1)
+            return x2.to(E4M3), torch.zeros(1, device=xf.device)
         amax = xf.abs().amax().reshape(1)
     else:
         if xf.numel() == 0:
-            return x2.to(E4M3), torch.zeros(xf.shape[0])
+            return x2.to(E4M3), torch.zeros(xf.shape[0], device=xf.device)
         amax = xf.abs().amax(dim=-1)
     s = torch.clamp(amax, min=1e-12) / FP8_MAX
     sb = s if mode == "tensor" else s[:, None]
@@ -215,19 +216,76 @@ def draft_block_mask(q_w, k_w, nheads, q_temporal, local, topk):
     return (flat > thr).reshape(nheads, NQ, NK)
 
 
+def block_mean_ordered(x_w):
+    """fp32 window means [N, C] of x_w [N, 128, C] in one fixed summation order (the
+    order the device pooling uses, so both give the same bits): partial sum g adds tokens
+    g, g+4, ..., g+124 in turn; mean = ((p0 + p1) + (p2 + p3)) / 128."""
+    xf = x_w.float()
+    N, S, C = xf.shape
+    g = xf.reshape(N, S // 4, 4, C)  # token 4*i + g
+    p = torch.zeros(N, 4, C, dtype=torch.float32, device=xf.device)
+    for i in range(S // 4):
+        p = p + g[:, i]
+    return ((p[:, 0] + p[:, 1]) + (p[:, 2] + p[:, 3])) / float(S)
+
+
+def _dots_ordered(aq, ak):
+    """[H, NQ, d] x [H, NK, d] -> [H, NQ, NK] fp32 dot products summed in ascending
+    channel order, each product and each sum rounded on its own (no fused multiply-add)."""
+    acc = torch.zeros(aq.shape[0], aq.shape[1], ak.shape[1], dtype=torch.float32, device=aq.device)
+    for e in range(aq.shape[2]):
+        acc = acc + aq[:, :, e, None] * ak[:, None, :, e]
+    return acc
+
+
+def draft_block_mask_ordered(q_w, k_w, nheads, q_temporal, local, topk):
+    """draft_block_mask (lcsa/reference.py:37-64) with every fp32 reduction in one stated
+    order, the contract the device builder meets bit for bit.  The rounding chain is the
+    reference's: bf16 window means, bf16 scores, bf16 / sqrt(d) -> bf16, -inf outside the
+    local mask, softmax to bf16, joint top-k per (head, query time row) with a strict `>`
+    threshold.  The orders where the reference leaves them to torch: means as in
+    block_mean_ordered; dots in ascending channel order; exp taken in double and rounded
+    to fp32; the softmax total summed over keys in ascending order; prob = e / total."""
+    NQ, _, C = q_w.shape
+    NK = k_w.shape[0]
+    d = C // nheads
+    aq = block_mean_ordered(q_w).to(torch.bfloat16).float().reshape(NQ, nheads, d).permute(1, 0, 2)
+    ak = block_mean_ordered(k_w).to(torch.bfloat16).float().reshape(NK, nheads, d).permute(1, 0, 2)
+    sqrt_d = torch.tensor(math.sqrt(d), dtype=torch.float32)
+    scores = (_dots_ordered(aq, ak).to(torch.bfloat16).float() / sqrt_d).to(torch.bfloat16).float()
+    sq, sk = local.shape
+    lm = local.to(scores.device).repeat(NQ // sq, NK // sk)
+    scores = scores.masked_fill(~lm[None], float("-inf"))
+    m = scores.amax(dim=-1, keepdim=True)
+    e = torch.where(torch.isinf(scores), torch.zeros_like(scores),
+                    torch.exp((scores - m).double()).float())
+    tot = torch.zeros(nheads, NQ, dtype=torch.float32, device=scores.device)
+    for j in range(NK):
+        tot = tot + e[:, :, j]
+    prob = (e / tot[..., None]).to(torch.bfloat16).float()
+    per_row = NQ // q_temporal
+    flat = prob.reshape(nheads * q_temporal, per_row * NK)
+    k = min(flat.shape[1] - 1, topk)
+    thr = torch.topk(flat, k=k + 1, dim=1).values[:, -1:]
+    return (flat > thr).reshape(nheads, NQ, NK)
+
+
 def causal_topk_mask(q_w, k_w, nheads, per_row, ratio):
     """Benchmark keep rule (synthetic causal rule of the attention configuration).
 
     Query block i sits in time row (NK-NQ)/per_row + i//per_row, key block j in row
     j//per_row.  Keep the query's own time row, plus the floor(ratio*#past) past blocks
     with the largest mean-pooled q.k score (ties -> lower index), never a future row.
+    The rule is this pack's own (no reference counterpart), so its fp32 evaluation order
+    is part of its definition: fp32 window means as block_mean_ordered, dots summed in
+    ascending channel order without fused multiply-adds.
     """
     NQ, _, C = q_w.shape
     NK = k_w.shape[0]
     d = C // nheads
-    aq = q_w.float().mean(dim=1).reshape(NQ, nheads, d).permute(1, 0, 2)
-    ak = k_w.float().mean(dim=1).reshape(NK, nheads, d).permute(1, 0, 2)
-    sc = torch.matmul(aq, ak.transpose(1, 2))  # [H, NQ, NK]
+    aq = block_mean_ordered(q_w).reshape(NQ, nheads, d).permute(1, 0, 2)
+    ak = block_mean_ordered(k_w).reshape(NK, nheads, d).permute(1, 0, 2)
+    sc = _dots_ordered(aq, ak).cpu().tolist()  # [H][NQ][NK] python floats
     keep = torch.zeros(nheads, NQ, NK, dtype=torch.bool)
     cache_rows = (NK - NQ) // per_row
     for i in range(NQ):
@@ -237,7 +295,8 @@ def causal_topk_mask(q_w, k_w, nheads, per_row, ratio):
         nsel = int(math.floor(ratio * npast))
         if nsel > 0:
             for h in range(nheads):
-                order = sorted(range(npast), key=lambda j: (-float(sc[h, i, j]), j))
+                row_sc = sc[h][i]
+                order = sorted(range(npast), key=lambda j: (-row_sc[j], j))
                 keep[h, i, order[:nsel]] = True
     return keep
 
@@ -251,11 +310,13 @@ def build_csr(keep):
     return order.to(torch.int32), cnt
 
 
-def sparse_attention(q_w, k_w, v_w, keep):
+def sparse_attention(q_w, k_w, v_w, keep, pairs=None):
     """sparse_attention_ref (lcsa/reference.py:67-88): fp32, per (head, query block).
 
     q_w [NQ, S, H*d], k_w/v_w [NK, S, H*d]; keep [H, NQ, NK].  Rows whose selection is
-    empty return 0 (the kernel's convention, triton_lcsa.py:57-59).
+    empty return 0 (the kernel's convention, triton_lcsa.py:57-59).  `pairs` (a list of
+    (head, query block)) evaluates only those pairs and leaves the rest 0, for checks of a
+    sample of a large problem.
     """
     NQ, S, C = q_w.shape
     H = keep.shape[0]
@@ -265,24 +326,24 @@ def sparse_attention(q_w, k_w, v_w, keep):
     k = k_w.float().reshape(-1, S, H, d).permute(2, 0, 1, 3)
     v = v_w.float().reshape(-1, S, H, d).permute(2, 0, 1, 3)
     out = torch.zeros_like(q)
-    for h in range(H):
-        for i in range(NQ):
-            sel = keep[h, i].nonzero(as_tuple=True)[0]
-            if sel.numel() == 0:
-                continue
-            kk = k[h, sel].reshape(-1, d)
-            vv = v[h, sel].reshape(-1, d)
-            p = torch.softmax(q[h, i] @ kk.t() * scale, dim=-1)
-            out[h, i] = p @ vv
+    todo = pairs if pairs is not None else [(h, i) for h in range(H) for i in range(NQ)]
+    for h, i in todo:
+        sel = keep[h, i].nonzero(as_tuple=True)[0]
+        if sel.numel() == 0:
+            continue
+        kk = k[h, sel].reshape(-1, d)
+        vv = v[h, sel].reshape(-1, d)
+        p = torch.softmax(q[h, i] @ kk.t() * scale, dim=-1)
+        out[h, i] = p @ vv
     return out.permute(1, 2, 0, 3).reshape(NQ, S, C)
 
 
 def _online_pass(qi, kh, vh, blocks, c, kv_len, lazy, S, d):
     """Online softmax over the key blocks `blocks` in the given order; returns (m, l, acc)
     with m the max the exponentials were taken against (log2 units, -inf if none)."""
-    m = torch.full((S,), float("-inf"))
-    l = torch.zeros(S)
-    acc = torch.zeros(S, d)
+    m = torch.full((S,), float("-inf"), device=qi.device)
+    l = torch.zeros(S, device=qi.device)
+    acc = torch.zeros(S, d, device=qi.device)
     for j in blocks:
         s = (qi @ kh[j].t()) * c
         if kv_len is not None and (j + 1) * S > kv_len:
@@ -303,15 +364,9 @@ def _online_pass(qi, kh, vh, blocks, c, kv_len, lazy, S, d):
     return m, l, acc
 
 
-def sparse_attention_online(q_w, k_w, v_w, keep, kv_len=None, lazy=0.0):
-    """The reference kernel's evaluation order (lcsa/triton_lcsa.py:44-59): per (head, query
-    block), kept key blocks in ascending order, online softmax in the log2 domain with fp32
-    running max / sum, P rounded to bf16 before P.V (`p.to(V.dtype)`), fp32 accumulator,
-    empty rows -> 0.  Keys at index >= kv_len are masked.  Returns fp32 [NQ, S, H*d].
-
-    lazy > 0 restates the B200 kernel's variant: the max the exponentials are taken against
-    is only raised when a block's max exceeds it by more than `lazy` (log2 units), and the
-    accumulator / sum are rescaled only then (same softmax, P rounded at another scale)."""
+def sparse_attention_online_loop(q_w, k_w, v_w, keep, kv_len=None, lazy=0.0):
+    """sparse_attention_online one (head, query block) at a time (the plain statement; the
+    batched form below must agree with it)."""
     NQ, S, C = q_w.shape
     H = keep.shape[0]
     d = C // H
@@ -329,18 +384,73 @@ def sparse_attention_online(q_w, k_w, v_w, keep, kv_len=None, lazy=0.0):
     return out.permute(1, 2, 0, 3).reshape(NQ, S, C)
 
 
+def sparse_attention_online(q_w, k_w, v_w, keep, kv_len=None, lazy=0.0):
+    """The reference kernel's evaluation order (lcsa/triton_lcsa.py:44-59): per (head, query
+    block), kept key blocks in ascending order, online softmax in the log2 domain with fp32
+    running max / sum, P rounded to bf16 before P.V (`p.to(V.dtype)`), fp32 accumulator,
+    empty rows -> 0.  Keys at index >= kv_len are masked.  Returns fp32 [NQ, S, H*d].
+
+    lazy > 0 restates the B200 kernel's variant: the max the exponentials are taken against
+    is only raised when a block's max exceeds it by more than `lazy` (log2 units), and the
+    accumulator / sum are rescaled only then (same softmax, P rounded at another scale).
+
+    Evaluated for all (head, query block) pairs at once: step j takes every pair's j-th
+    kept key block (ascending), and pairs with fewer kept blocks see an all -inf block,
+    which leaves their running max, sum and accumulator exactly unchanged.  Runs on the
+    device of q_w."""
+    NQ, S, C = q_w.shape
+    H = keep.shape[0]
+    d = C // H
+    dev = q_w.device
+    c = (1.0 / math.sqrt(d)) * 1.4426950408889634
+    q = q_w.float().reshape(NQ, S, H, d).permute(2, 0, 1, 3)  # [H, NQ, S, d]
+    k = k_w.float().reshape(-1, S, H, d).permute(2, 0, 1, 3)  # [H, NK, S, d]
+    v = v_w.float().reshape(-1, S, H, d).permute(2, 0, 1, 3)
+    keep = keep.to(dev)
+    cnt = keep.sum(-1)  # [H, NQ]
+    maxc = int(cnt.max().item()) if cnt.numel() else 0
+    order = torch.argsort((~keep).to(torch.int8), dim=-1, stable=True)  # kept ids ascending first
+    hidx = torch.arange(H, device=dev)[:, None]
+    cols = torch.arange(S, device=dev)
+    ninf = float("-inf")
+    m = torch.full((H, NQ, S), ninf, device=dev)
+    l = torch.zeros(H, NQ, S, device=dev)
+    acc = torch.zeros(H, NQ, S, d, device=dev)
+    for j in range(maxc):
+        kj = order[:, :, j]  # [H, NQ]
+        s = torch.matmul(q, k[hidx, kj].transpose(-1, -2)) * c  # [H, NQ, S, S]
+        valid = (j < cnt)[..., None, None]
+        if kv_len is not None:
+            valid = valid & ((kj[..., None] * S + cols) < kv_len)[..., None, :]
+        s = torch.where(valid, s, torch.full_like(s, ninf))
+        mb = s.amax(dim=-1)
+        if lazy > 0:
+            m_new = torch.where(mb > m + lazy, mb, m)
+        else:
+            m_new = torch.maximum(m, mb)
+        safe = torch.where(torch.isinf(m_new), torch.zeros_like(m_new), m_new)
+        alpha = torch.where(torch.isinf(m_new), torch.ones_like(m),
+                            torch.where(torch.isinf(m), torch.zeros_like(m), torch.exp2(m - safe)))
+        p = torch.exp2(s - safe[..., None])
+        l = l * alpha + p.sum(dim=-1)
+        acc = acc * alpha[..., None] + torch.matmul(p.to(torch.bfloat16).float(), v[hidx, kj])
+        m = m_new
+    out = torch.where(l[..., None] > 0, acc / l.clamp(min=1e-30)[..., None], torch.zeros_like(acc))
+    return out.permute(1, 2, 0, 3).reshape(NQ, S, C)
+
+
 def dense_attention_online(q, k, v, nheads, lazy=0.0):
     """Dense attention in the kernel's order: every key block kept (cross-attention)."""
     Lq, C = q.shape
     Lk = k.shape[0]
     nq, nk = -(-Lq // 128), -(-Lk // 128)
-    qp = torch.zeros(nq * 128, C, dtype=q.dtype)
+    qp = torch.zeros(nq * 128, C, dtype=q.dtype, device=q.device)
     qp[:Lq] = q
-    kp = torch.zeros(nk * 128, C, dtype=k.dtype)
+    kp = torch.zeros(nk * 128, C, dtype=k.dtype, device=q.device)
     kp[:Lk] = k
-    vp = torch.zeros(nk * 128, C, dtype=v.dtype)
+    vp = torch.zeros(nk * 128, C, dtype=v.dtype, device=q.device)
     vp[:Lk] = v
-    keep = torch.ones(nheads, nq, nk, dtype=torch.bool)
+    keep = torch.ones(nheads, nq, nk, dtype=torch.bool, device=q.device)
     o = sparse_attention_online(qp.view(nq, 128, C), kp.view(nk, 128, C), vp.view(nk, 128, C),
                                 keep, kv_len=Lk, lazy=lazy)
     return o.reshape(nq * 128, C)[:Lq]

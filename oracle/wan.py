@@ -198,6 +198,21 @@ def standin_state_dict(P):
     return {k: v.to(torch.bfloat16) for k, v in sd.items()}
 
 
+def params_from_state_dict(sd):
+    """Inverse of standin_state_dict: a Wan DiTBlock state dict -> block params P (the
+    tensors keep their dtype and device, so the oracle quantises the very weights the
+    module holds)."""
+    P = {"modulation": sd["modulation"]}
+    for part, prefix in (("self", "self_attn"), ("cross", "cross_attn")):
+        P[part] = {n: (sd[f"{prefix}.{n}.weight"], sd[f"{prefix}.{n}.bias"]) for n in ("q", "k", "v", "o")}
+        P[part]["norm_q"] = sd[f"{prefix}.norm_q.weight"]
+        P[part]["norm_k"] = sd[f"{prefix}.norm_k.weight"]
+    P["norm3"] = (sd["norm3.weight"], sd["norm3.bias"])
+    P["ffn0"] = (sd["ffn.0.weight"], sd["ffn.0.bias"])
+    P["ffn2"] = (sd["ffn.2.weight"], sd["ffn.2.bias"])
+    return P
+
+
 def causal_mask_fn(nheads, per_row, ratio=0.25):
     return lambda q_w, k_w: O.causal_topk_mask(q_w, k_w, nheads, per_row, ratio)
 

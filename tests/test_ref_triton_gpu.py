@@ -1,0 +1,94 @@
+"""This pack's kernels against the reference's own GPU kernels (its Triton kernels and its
+cuBLASLt _scaled_mm call), run on a B200 by tests/golden/make_golden_triton.py and saved
+with their inputs in tests/golden/triton_b200.pt.
+
+Bars: FP8 codes and scales bit-exact, gate-add bitwise, RMSNorm+RoPE / LN-modulate within
+one bf16 ulp (of the result or of the operands of the last add), attention at the
+reference test's atol = rtol = 1e-2 (lcsa/test_correctness.py:59), the FP8 GEMM within
+1e-2 max relative error."""
+import os
+
+import pytest
+import torch
+
+from oracle import ops as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+FIX = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "triton_b200.pt")
+
+
+@pytest.fixture(scope="module")
+def fx():
+    if not os.path.exists(FIX):
+        pytest.skip("tests/golden/triton_b200.pt not generated yet")
+    return torch.load(FIX, weights_only=False)
+
+
+def _ulp(t):
+    mag = t.float().abs().clamp(min=2.0 ** -126)
+    return torch.pow(2.0, torch.floor(torch.log2(mag)) - 7)
+
+
+def _within_one_ulp(out, ref, operand):
+    out, ref = out.float().cpu(), ref.float().cpu()
+    tol = _ulp(torch.maximum(out.abs(), ref.abs())) + _ulp(operand.float().cpu())
+    return bool(((out - ref).abs() <= tol).all())
+
+
+@pytest.mark.parametrize("case", ["quant", "quant_mid", "quant_edge0", "quant_edge1", "quant_edge2"])
+def test_quant_codes_equal_reference_triton(fx, case):
+    from flashvsr_sm89_ops_b200 import quantize_fp8
+    c = fx[case]
+    q, s = quantize_fp8(c["x"].to(DEV), "tensor")
+    assert torch.equal(s.cpu().reshape(-1), c["scale"].reshape(-1))
+    diff = (q.view(torch.uint8).cpu() != c["q"])
+    assert not diff.any(), f"{int(diff.sum())} codes differ"
+
+
+def test_gelu_quant_equals_reference_triton(fx):
+    from flashvsr_sm89_ops_b200.fp8_quant import fused_gelu_quant_fp8
+    c = fx["gelu_quant"]
+    q, s = fused_gelu_quant_fp8(c["h"].to(DEV), "tensor")
+    assert torch.equal(s.cpu().reshape(-1), c["scale"].reshape(-1))
+    d = (q.view(torch.uint8).cpu().to(torch.int16) - c["q"].to(torch.int16)).abs()
+    assert int((d != 0).sum()) == 0, f"{int((d != 0).sum())} of {d.numel()} codes differ"
+
+
+def test_rms_rope_equals_reference_triton(fx):
+    from flashvsr_sm89_ops_b200 import fused_rms_rope
+    c = fx["rms_rope"]
+    y = fused_rms_rope(c["x"].to(DEV), c["w"].to(DEV), c["freqs"].to(DEV), eps=1e-6, rope=True)
+    y0 = fused_rms_rope(c["x"].to(DEV), c["w"].to(DEV), None, eps=1e-6, rope=False)
+    assert torch.equal(y0.cpu(), c["y_norope"]) or _within_one_ulp(y0, c["y_norope"], c["y_norope"])
+    assert _within_one_ulp(y, c["y"], c["y_norope"])
+
+
+def test_ln_modulate_and_gate_add_equal_reference_triton(fx):
+    from flashvsr_sm89_ops_b200 import fused_gate_add, fused_ln_modulate
+    c = fx["adaln"]
+    y = fused_ln_modulate(c["x"].to(DEV), c["scale"].to(DEV), c["shift"].to(DEV), eps=1e-6)
+    assert _within_one_ulp(y, c["y"], c["shift"].expand_as(c["y"]).abs() + c["y"].abs())
+    ga = fused_gate_add(c["x"].to(DEV), c["gate"].to(DEV), c["r"].to(DEV))
+    assert torch.equal(ga.cpu(), c["gate_add"])
+
+
+def test_attention_equals_reference_triton(fx):
+    from flashvsr_sm89_ops_b200.lcsa import block_sparse_attention
+    c = fx["attention"]
+    o = block_sparse_attention(c["q"].to(DEV), c["k"].to(DEV), c["v"].to(DEV), c["keep"].to(DEV))
+    assert torch.allclose(o.float().cpu(), c["out"].float(), atol=1e-2, rtol=1e-2)
+
+
+def test_fp8_gemm_equals_reference_cublaslt(fx):
+    from flashvsr_sm89_ops_b200.fp8_linear import fp8_mm
+    c = fx["scaled_mm"]
+    y = fp8_mm(c["x8"].view(torch.float8_e4m3fn).to(DEV), c["x_scale"].to(DEV).reshape(1),
+               c["w8"].view(torch.float8_e4m3fn).to(DEV), c["w_scale"].to(DEV).reshape(1),
+               c["b"].to(DEV))
+    ref = c["y"].float()
+    assert ((y.float().cpu() - ref).abs().max() / ref.abs().max()).item() < 1e-2
+    # the oracle's restated _mm agrees with cuBLASLt to an fp32 accumulation order
+    yo = O.fp8_mm(c["x8"].view(torch.float8_e4m3fn), c["x_scale"], c["w8"].view(torch.float8_e4m3fn),
+                  c["w_scale"], c["b"])
+    assert _within_one_ulp(yo, c["y"], c["y"])
