@@ -110,6 +110,16 @@ __device__ __forceinline__ float gelu_tanh_bf16(float x) {
   return bf16r(0.5f * x * (1.0f + tanhf(inner)));
 }
 
+// The scale returned beside the codes, the reference's `amax / FP8_MAX` (fp8_quant.py:54,
+// fp8_ffn.py:72) as torch evaluates it on a CUDA tensor: a division by a host scalar runs as
+// a multiply by the scalar's fp32 reciprocal, fl(amax * fl(1/448)).  (Measured on a B200:
+// the reference's returned scale equals this and differs from the IEEE quotient by one ulp
+// for some amax.)  The scale the codes are divided by, max(amax, 1e-12) / 448, is an IEEE
+// divide inside the reference's kernel and stays one here.
+__device__ __forceinline__ float returned_scale(float amax) {
+  return __fmul_rn(amax, 1.0f / 448.0f);
+}
+
 __device__ __noinline__ uint2 e4m3x8_exact(float f0, float f1, float f2, float f3, float f4,
                                            float f5, float f6, float f7, float s) {
   const uint32_t c0 = f32x2_to_e4m3x2(__fdiv_rn(f0, s), __fdiv_rn(f1, s));

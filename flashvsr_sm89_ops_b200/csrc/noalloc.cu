@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(256) quant_from_partials_kernel(
   // s = max(amax, 1e-12) / 448, q = e4m3(clamp(x / s)), IEEE divides (fp8_quant.py:25-35);
   // the saturating conversion is the clamp and, like clamp-then-cast, keeps a NaN a NaN
   const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
-  if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = __fdiv_rn(amax, 448.0f);
+  if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = returned_scale(amax);
   const int64_t nvec = n >> 3;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
   uint2* qv = reinterpret_cast<uint2*>(q);

@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_k
         const int v = j * 32 + lane;
         if (v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
       }
-      if (lane == 0) q_scale[row] = __fdiv_rn(amax, 448.0f);
+      if (lane == 0) q_scale[row] = returned_scale(amax);
     }
   };
   if (GATE) {
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(256, 2) layer_norm_kernel(
         const int v = j * 32 + lane;
         if (v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
       }
-      if (lane == 0) q_scale[row] = __fdiv_rn(amax, 448.0f);
+      if (lane == 0) q_scale[row] = returned_scale(amax);
     }
   };
   if (GATE) {

@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(256) quant_tensor_kernel(
   const float amax = *amax_p;
   const float s = quant_scale_from_amax(amax);
   const float rs = __frcp_rn(s);
-  if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = __fdiv_rn(amax, kFp8Max);
+  if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = returned_scale(amax);
   for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
        v += (int64_t)gridDim.x * blockDim.x) {
     float f[8];
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(256, kRowBlocksPerSM) quant_row_kernel(
         qv[j * 32 + lane] = quant8(f, s, rs);
       }
     }
-    if (lane == 0) scale_out[row] = __fdiv_rn(m, kFp8Max);
+    if (lane == 0) scale_out[row] = returned_scale(m);
   };
   row_pipeline<NV>(M, load, body);
 }
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(256) quant_row_long_kernel(const __nv_bfloat16
     load8<GELU>(xv, v, f);
     qv[v] = quant8(f, s, rs);
   }
-  if (lane == 0) scale_out[row] = __fdiv_rn(m, kFp8Max);
+  if (lane == 0) scale_out[row] = returned_scale(m);
 }
 
 // Quantisation with a precomputed amax (the second half of fused_gelu_quant_fp8,
@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(256, 4) quant_with_amax_kernel(
     const float a = __ldg(amax + (per_row ? row : 0));
     const float s = quant_scale_from_amax(a);
     const float rs = __frcp_rn(s);
-    if (lane == 0 && (per_row || row == 0)) scale_out[per_row ? row : 0] = __fdiv_rn(a, kFp8Max);
+    if (lane == 0 && (per_row || row == 0)) scale_out[per_row ? row : 0] = returned_scale(a);
     const uint4* gr = g + row * kv;
     uint2* qr = q + row * kv;
     int v = lane;

@@ -2,7 +2,8 @@
 
 Drop-in for ``flashvsr_sm89_ops.fp8_quant`` (fp8_quant.py:13-55): same name,
 same return convention ``(codes, scale)`` with ``scale = amax / 448`` kept on
-the GPU (no host sync).  ``mode="token"`` adds one scale per row.
+the GPU (no host sync), computed as the reference's torch expression evaluates on a CUDA
+tensor: ``amax * fl(1/448)``.  ``mode="token"`` adds one scale per row.
 """
 from __future__ import annotations
 
@@ -62,7 +63,8 @@ def _run(fn: str, x2: torch.Tensor, mode: str):
 def quantize_fp8(x2: torch.Tensor, mode: str = "tensor"):
     """x2: [M, K] bf16 -> (e4m3 codes [M, K], fp32 scale [1] or [M] on the GPU).
 
-    s = max(amax, 1e-12)/448; codes = e4m3(clamp(x/s, +-448)); returned scale = amax/448.
+    s = max(amax, 1e-12)/448; codes = e4m3(clamp(x/s, +-448)); returned scale =
+    amax * fl(1/448) (the reference's `amax / FP8_MAX` on a CUDA tensor).
     """
     return _run("fvb_quant_fp8", x2, mode)
 

@@ -59,7 +59,9 @@ FVB_API int fvb_device_error(unsigned int* code_out);
  * Replaces quantize_fp8(x2) (fp8_quant.py:42-55; kernels :16-35) and the
  * eager branch of FP8Linear.forward (fp8_linear.py:38-40).
  *   s = max(amax, 1e-12) / 448;  q = e4m3(clamp(x / s, -448, 448))  (IEEE divide, RNE)
- *   scale_out = amax / 448  (fp32; [1] for FVB_SCALE_TENSOR, [M] for FVB_SCALE_ROW)
+ *   scale_out = amax * fl(1/448)  (fp32; [1] for FVB_SCALE_TENSOR, [M] for FVB_SCALE_ROW):
+ *   the reference's returned `amax / FP8_MAX` as torch computes it on a CUDA tensor (a
+ *   division by a host scalar is a multiply by the scalar's fp32 reciprocal)
  * x [M,K] bf16, q [M,K] fp8.  FVB_SCALE_TENSOR needs `workspace` of
  * fvb_quant_fp8_workspace_bytes() bytes (device, 16-byte aligned); FVB_SCALE_ROW needs none.
  * M*K == 0 writes scale 0 like the reference (fp8_quant.py:45-47). */
@@ -108,7 +110,7 @@ FVB_API int fvb_fp8_gemm(const void* A, const float* sa, int a_mode, const void*
                  int epilogue, float* amax_out, fvb_stream_t stream);
 
 /* Quantise with a precomputed amax (second half of the FFN mid-section):
- *   s = max(amax,1e-12)/448, q = e4m3(clamp(g/s)), scale_out = amax/448. */
+ *   s = max(amax,1e-12)/448, q = e4m3(clamp(g/s)), scale_out = amax * fl(1/448). */
 FVB_API int fvb_quant_fp8_with_amax(const void* g, int64_t M, int64_t K, const float* amax, int mode,
                             void* q, float* scale_out, fvb_stream_t stream);
 

@@ -16,12 +16,24 @@ FP8_MAX = 448.0  # flashvsr_sm89_ops/fp8_quant.py:13
 E4M3 = torch.float8_e4m3fn
 
 
+def div_ieee(a, b):
+    """a / b as the IEEE fp32 quotient on every device.  Evaluated in float64 and rounded to
+    float32, which is exactly the correctly rounded fp32 quotient (binary64 carries more than
+    2*24 + 2 bits, so the second rounding is innocuous).  A divisor given as a number is made
+    a tensor first: torch's CUDA kernels turn a division by a host scalar into a multiply by
+    its reciprocal, which is not the quotient (and moves exact e4m3 ties)."""
+    if not torch.is_tensor(b):
+        b = torch.tensor(float(b), dtype=torch.float64, device=a.device)
+    return (a.double() / b.double()).float()
+
+
 # ----------------------------------------------------------------------------- FP8
 def quantize_fp8(x2: torch.Tensor, mode: str = "tensor"):
     """Activation quantisation of flashvsr_sm89_ops/fp8_quant.py:42-55 (kernels :16-35).
 
     amax = max|x| (fp32); s = max(amax, 1e-12)/448; q = e4m3(clamp(x/s, +-448)) with an
-    fp32 IEEE divide and round-to-nearest-even; the returned scale is amax/448.
+    fp32 IEEE divide and round-to-nearest-even; the returned scale is returned_scale(amax),
+    i.e. amax/448 as a multiply by fl(1/448).
     mode "token" applies the same formula to each row (the per-token granularity the
     B200 pack adds; no reference counterpart beyond the formula).
     """
@@ -34,10 +46,24 @@ def quantize_fp8(x2: torch.Tensor, mode: str = "tensor"):
         if xf.numel() == 0:
             return x2.to(E4M3), torch.zeros(xf.shape[0], device=xf.device)
         amax = xf.abs().amax(dim=-1)
-    s = torch.clamp(amax, min=1e-12) / FP8_MAX
+    s = div_ieee(torch.clamp(amax, min=1e-12), FP8_MAX)
     sb = s if mode == "tensor" else s[:, None]
-    q = torch.clamp(xf / sb, -FP8_MAX, FP8_MAX).to(E4M3)
-    return q, amax / FP8_MAX
+    q = torch.clamp(div_ieee(xf, sb), -FP8_MAX, FP8_MAX).to(E4M3)
+    return q, returned_scale(amax)
+
+
+# fp32 reciprocal of FP8_MAX, as torch forms it for a division of a CUDA tensor by a host scalar
+INV_FP8_MAX = torch.tensor(1.0, dtype=torch.float32) / FP8_MAX
+
+
+def returned_scale(amax):
+    """The scale quantize_fp8 returns, `amax / FP8_MAX` (fp8_quant.py:54), as it evaluates on
+    the reference's platform: torch divides a CUDA tensor by a host scalar as a multiply by
+    the scalar's fp32 reciprocal, fl(amax * fl(1/448)).  Pinned by the reference's own
+    quantize_fp8 run on a B200 (tests/golden/triton_b200.pt), whose returned scale differs
+    from the IEEE quotient by one ulp for some amax; CPU torch divides exactly, so the
+    product is spelled out."""
+    return amax.float() * INV_FP8_MAX.to(amax.device)
 
 
 def gelu_tanh(h: torch.Tensor) -> torch.Tensor:
@@ -117,8 +143,8 @@ def rms_rope(x, weight, cos=None, sin=None, eps=1e-6, rope=True, head_dim=128):
     """
     B, L, D = x.shape
     xf = x.float()
-    ms = (xf * xf).sum(-1, keepdim=True) / D
-    rrms = 1.0 / torch.sqrt(ms + eps)
+    ms = div_ieee((xf * xf).sum(-1, keepdim=True), D)
+    rrms = div_ieee(torch.ones_like(ms), torch.sqrt(ms + eps))
     y = (xf * rrms).to(torch.bfloat16).float() * weight.float()
     if not rope:
         return y.to(torch.bfloat16)
@@ -140,9 +166,9 @@ def ln_modulate(x, scale, shift, eps=1e-6):
     """
     xf = x.float()
     D = x.shape[-1]
-    mean = xf.sum(-1, keepdim=True) / D
-    var = ((xf - mean) ** 2).sum(-1, keepdim=True) / D
-    xn = ((xf - mean) / torch.sqrt(var + eps)).to(torch.bfloat16).float()
+    mean = div_ieee(xf.sum(-1, keepdim=True), D)
+    var = div_ieee(((xf - mean) ** 2).sum(-1, keepdim=True), D)
+    xn = div_ieee(xf - mean, torch.sqrt(var + eps)).to(torch.bfloat16).float()
     one_plus = (1.0 + scale.float()).to(torch.bfloat16).float()
     y = (xn * one_plus).to(torch.bfloat16).float()
     return (y + shift.float()).to(torch.bfloat16)

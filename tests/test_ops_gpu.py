@@ -60,6 +60,33 @@ def test_quantize_fp8_bitexact(M, K, mode):
     assert torch.equal(s.cpu(), sr.float())
 
 
+@pytest.mark.parametrize("M,K", [(8448, 1536), (16896, 1536), (8448, 8960)])
+@pytest.mark.parametrize("mode", ["tensor", "token"])
+def test_quantize_fp8_bitexact_step_shapes(M, K, mode):
+    """The step's row counts: every warp of the per-token kernel carries several rows (its
+    two-row pipeline), which the small shapes above never reach."""
+    from flashvsr_sm89_ops_b200 import quantize_fp8
+    x = O.fp8_outlier_activations(M, K, gen(M + 2 * K))
+    q, s = quantize_fp8(x.to(DEV), mode)
+    qr, sr = O.quantize_fp8(x, mode)
+    assert torch.equal(q.view(torch.uint8).cpu(), qr.view(torch.uint8))
+    assert torch.equal(s.cpu(), sr.float())
+
+
+@pytest.mark.parametrize("mode", ["tensor", "token"])
+def test_oracle_on_gpu_quantizes_like_oracle_on_cpu(mode):
+    """The block-level checks evaluate the oracle's torch code on the GPU; its quantisation
+    must give the CPU oracle's codes and scales bit for bit (a division by a host scalar on
+    a CUDA tensor is a reciprocal multiply, which div_ieee keeps out)."""
+    g = gen(77)
+    x = (torch.randn(8448, 1536, generator=g) * 3).to(torch.bfloat16)
+    x[::5, 0] = 7.0 * 2.0 ** torch.randint(-2, 4, (x[::5].shape[0],), generator=g).float()  # ties
+    qg, sg = O.quantize_fp8(x.to(DEV), mode)
+    qc, sc = O.quantize_fp8(x, mode)
+    assert torch.equal(qg.view(torch.uint8).cpu(), qc.view(torch.uint8))
+    assert torch.equal(sg.cpu(), sc)
+
+
 def _near_midpoint_rows(rows, K, seed):
     """bf16 rows whose quotients x / s (s = row amax / 448, the reference's fp32 IEEE
     divide) sit on or next to e4m3 rounding midpoints or in the e4m3 subnormal range.
@@ -337,7 +364,10 @@ def test_fp8_gemm_bench_shapes(M, N, K, mode):
     rows = torch.unique(torch.cat([rows, torch.tensor([0, M - 1])]))
     sxr = sx.cpu()[rows] if mode == "token" else sx.cpu()
     ref = O.fp8_mm(qx[rows.to(DEV)].cpu(), sxr, qwr, swr, b.cpu())
-    assert max_rel(out[rows.to(DEV)], ref) < 1e-2
+    got = out[rows.to(DEV)]
+    assert max_rel(got, ref) < 1e-2
+    # same codes on both sides: only fp32 summation order and the final bf16 rounding differ
+    assert (got.float().cpu() - ref.float()).norm().item() / ref.float().norm().item() < 1e-4
     assert torch.isfinite(out.float()).all()
 
 

@@ -130,7 +130,9 @@ def test_causal_rule_counts():
 def test_quantize_formula_edges():
     x = torch.tensor([[0.0, 1.0, -448.0 * 3, 2.0 ** -20]], dtype=torch.bfloat16)
     q, s = O.quantize_fp8(x, "tensor")
-    assert s.item() == pytest.approx(3.0, rel=0, abs=0)
+    # amax 1344: the returned scale is fl(1344 * fl(1/448)) = 3 + 2^-22, one ulp above the
+    # IEEE quotient 3 (the reference's GPU semantics, see returned_scale)
+    assert s.item() == 3.0 + 2.0 ** -22
     assert q.float()[0, 2].item() == -448.0
     z, sz = O.quantize_fp8(torch.zeros(2, 4, dtype=torch.bfloat16), "token")
     assert z.float().abs().max().item() == 0 and sz.abs().max().item() == 0
@@ -189,7 +191,23 @@ def test_oracle_adaln_equals_reference_triton():
     c = load("triton_b200.pt")["adaln"]
     y = O.ln_modulate(c["x"], c["scale"], c["shift"], 1e-6)
     assert _one_ulp(y, c["y"], c["shift"].expand_as(c["y"]).abs() + c["y"].abs())
-    assert torch.equal(O.gate_add(c["x"], c["gate"], c["r"]), c["gate_add"])
+
+
+@needs_triton
+def test_reference_triton_gate_add_skips_the_inner_rounding():
+    """The reference documents its gate-add kernel as bitwise equal to eager x + g * r, i.e.
+    bf16(x + bf16(g * r)) (fused_adaln.py:8-12, :53-57).  Run on a B200 with Triton 3.6 it
+    computes bf16(x + g * r) instead: the bf16 round trip of the product is gone (g * r of
+    two bf16 values is exact in fp32), and about 18% of the outputs sit one bf16 ulp from
+    eager.  The oracle (and the pack's kernel) keep the eager chain, the contract the
+    reference states; this pins what its Triton kernel does on this GPU."""
+    c = load("triton_b200.pt")["adaln"]
+    x, g, r = c["x"].float(), c["gate"].float(), c["r"].float()
+    assert torch.equal((x + g * r).to(torch.bfloat16), c["gate_add"])
+    eager = O.gate_add(c["x"], c["gate"], c["r"])
+    frac = (eager != c["gate_add"]).float().mean().item()
+    assert 0.05 < frac < 0.4, frac
+    assert ((eager.float() - c["gate_add"].float()).abs() <= _ulp(eager) + _ulp(g * r)).all()
 
 
 @needs_triton
