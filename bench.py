@@ -366,20 +366,59 @@ def tiled_4k(runner, world, rank, dev, dist_mod):
         dist_mod.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stream = torch.cuda.current_stream(dev)
+    tm = {}
     e0.record(stream)
-    out = render_tiled(pipe, lq, tile_target=700_000, tile_threshold=700_000, device=dev)
+    out = render_tiled(pipe, lq, tile_target=700_000, tile_threshold=700_000, device=dev,
+                       timings=tm)
     e1.record(stream)
     torch.cuda.synchronize(dev)
+    ev = tm["events"]
+    # this rank's split: its tiles (render + blend), the cross-rank reduce, crop-packing waits
+    part = torch.tensor([ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), tm["load_wait_s"] * 1e3,
+                         float(tm["tiles"])], device=dev, dtype=torch.float64)
     t = torch.tensor([e0.elapsed_time(e1), float(pipe.tokens)], device=dev, dtype=torch.float64)
+    parts = [part]
     if world > 1:
         tok = t[1:2].clone()
         dist_mod.all_reduce(t[0:1], op=dist_mod.ReduceOp.MAX)
         dist_mod.all_reduce(tok, op=dist_mod.ReduceOp.SUM)
         t[1] = tok[0]
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist_mod.all_gather(parts, part)
     ms, tokens = float(t[0].item()), float(t[1].item())
+    # the same canvas on one GPU in the same job (rank 0 alone, the others wait): the
+    # single-GPU time the strong-scaling efficiency is measured against
+    solo = None
+    if world > 1 and os.environ.get("FVB_SKIP_TILED_N1") != "1":
+        g0 = dist_mod.new_group([0])
+        if rank == 0:
+            pipe.tokens = 0
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            ref = render_tiled(pipe, lq, tile_target=700_000, tile_threshold=700_000, device=dev,
+                               group=g0)
+            s1.record(stream)
+            torch.cuda.synchronize(dev)
+            solo = {"ms": s0.elapsed_time(s1),
+                    "max_abs_diff_vs_sharded": float((ref.float() - out.float()).abs().max().item())}
+            del ref
+        dist_mod.barrier()
     if rank != 0:
         return None
     n_out = int(out.shape[1])
+    per_rank = [[float(v) for v in p.tolist()] for p in parts]
+    breakdown = {
+        "per_rank_tiles_ms": [round(p[0], 1) for p in per_rank],
+        "per_rank_reduce_ms": [round(p[1], 1) for p in per_rank],
+        "per_rank_crop_wait_ms": [round(p[2], 1) for p in per_rank],
+        "per_rank_tiles": [int(p[3]) for p in per_rank],
+        "canvas_reduce_bytes": int(out.numel()) * 4,
+    }
+    extra = {}
+    if solo is not None:
+        extra = {"n1_same_job_ms": solo["ms"], "n1_same_job_fps": n_out / (solo["ms"] / 1e3),
+                 "efficiency_vs_n1_same_job": solo["ms"] / (world * ms),
+                 "n1_max_abs_diff_vs_sharded": solo["max_abs_diff_vs_sharded"]}
     return {
         "fps": n_out / (ms / 1e3), "unit": "frames/s", "frames": n_out, "ms": ms,
         "canvas": f"{W4}x{H4}", "input_frames": frames_in, "tiles": len(tiles),
@@ -389,6 +428,7 @@ def tiled_4k(runner, world, rank, dev, dist_mod):
         "schedule": "per tile: f=6 chunk + 7 f=2 chunks (KV cache of 3 time rows), 30 blocks; "
                     "patch-embed / unpatchify are bf16 linears standing in for the LQ "
                     "projection and VAE",
+        "breakdown": breakdown, **extra,
     }
 
 

@@ -242,6 +242,25 @@ __device__ __forceinline__ void row_pipeline_prep(int64_t rows, Load load, Prep 
   }
 }
 
+// The schedule of row_pipeline_prep with the row held as fp32: prep(row, raw, f) turns the
+// arrived raw vectors into the lane's NV * 8 fp32 values (unpacked once per row) before the
+// next row's raw loads are issued into the same registers, so a lane holds 4 * NL + 8 * NV
+// registers of row data.
+template <int NV, int NL, typename Load, typename Prep, typename Body>
+__device__ __forceinline__ void row_pipeline_f(int64_t rows, Load load, Prep prep, Body body) {
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  uint4 raw[NL];
+  float f[NV * 8];
+  load(row, raw);
+  for (; row < rows; row += nwarps) {
+    prep(row, raw, f);
+    if (row + nwarps < rows) load(row + nwarps, raw);
+    body(row, f);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // shared-memory / mbarrier PTX
 // ---------------------------------------------------------------------------

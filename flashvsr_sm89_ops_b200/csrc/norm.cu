@@ -300,40 +300,49 @@ __global__ void __launch_bounds__(256) gate_add_kernel(const uint4* __restrict__
   }
 }
 
+template <int NV>
+__device__ __forceinline__ void unpack_row_f(const uint4* raw, float* f, int lane, int nvec) {
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+    if (j * 32 + lane < nvec) bf16x8_to_f32(raw[j], f + 8 * j);
+}
+
 // RMSNorm (+ interleaved RoPE).  y = bf16(x * rrms) * w in fp32 (an exact product of two
 // bf16 values); the rotation rounds each product and the sum once, all in packed fp32 pairs
-// (mul.rn / add.rn per lane, no contraction), then one bf16 rounding.
+// (mul.rn / add.rn per lane, no contraction), then one bf16 rounding.  rrms =
+// rsqrt(sum(x^2) / D + eps) with the approximate reciprocal square root, as the reference's
+// Triton kernel takes it (tl.rsqrt).
 template <bool ROPE, int NV>
-__global__ void __launch_bounds__(256, kRowBlocksPerSM) rms_rope_kernel(
+__global__ void __launch_bounds__(256, 2) rms_rope_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t x_ld, const __nv_bfloat16* __restrict__ w,
     const float* __restrict__ cosv, const float* __restrict__ sinv, int64_t rows, int64_t L,
     int D, int head_dim, float eps, const int32_t* __restrict__ row_map,
     __nv_bfloat16* __restrict__ out) {
   const int lane = threadIdx.x & 31;
   const int nvec = D >> 3;
-  auto load = [&](int64_t row, uint4* xr) {
+  const float invD = 1.0f / (float)D;
+  auto load = [&](int64_t row, uint4* raw) {
     const uint4* xv = reinterpret_cast<const uint4*>(x + row * x_ld);
 #pragma unroll
     for (int j = 0; j < NV; ++j)
-      if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+      if (j * 32 + lane < nvec) raw[j] = __ldg(xv + j * 32 + lane);
   };
-  auto body = [&](int64_t row, uint4* xr) {
+  auto prep = [&](int64_t, const uint4* raw, float* f) { unpack_row_f<NV>(raw, f, lane, nvec); };
+  auto body = [&](int64_t row, float* f) {
     uint64_t q2 = f2_pack(0.f, 0.f);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       if (j * 32 + lane < nvec) {
-        float f[8];
-        bf16x8_to_f32(xr[j], f);
 #pragma unroll
         for (int i = 0; i < 8; i += 2) {
-          const uint64_t t = f2_pack(f[i], f[i + 1]);
+          const uint64_t t = f2_pack(f[8 * j + i], f[8 * j + i + 1]);
           q2 = f2_fma(t, t, q2);
         }
       }
     }
     float qa, qb;
     f2_unpack(q2, qa, qb);
-    const float rrms = __frsqrt_rn(__fdiv_rn(warp_sum(qa + qb), (float)D) + eps);
+    const float rrms = rsqrtf(warp_sum(qa + qb) * invD + eps);
     const uint64_t rr = f2_pack(rrms, rrms);
     const int64_t srow = row % L;
     const int half = head_dim >> 1;
@@ -343,8 +352,7 @@ __global__ void __launch_bounds__(256, kRowBlocksPerSM) rms_rope_kernel(
     for (int j = 0; j < NV; ++j) {
       const int v = j * 32 + lane;
       if (v < nvec) {
-        float f[8], wf[8];
-        bf16x8_to_f32(xr[j], f);
+        float wf[8];
         bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), wf);
         float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f), s4 = c4;
         if (ROPE) {
@@ -359,17 +367,20 @@ __global__ void __launch_bounds__(256, kRowBlocksPerSM) rms_rope_kernel(
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
           float a, b;
-          f2_unpack(f2_mul(f2_pack(f[2 * p], f[2 * p + 1]), rr), a, b);
+          f2_unpack(f2_mul(f2_pack(f[8 * j + 2 * p], f[8 * j + 2 * p + 1]), rr), a, b);
           const float2 yb = __bfloat1622float2(__floats2bfloat162_rn(a, b));
-          float ye, yo_;
-          f2_unpack(f2_mul(f2_pack(yb.x, yb.y), f2_pack(wf[2 * p], wf[2 * p + 1])), ye, yo_);
+          const uint64_t yw = f2_mul(f2_pack(yb.x, yb.y), f2_pack(wf[2 * p], wf[2 * p + 1]));
           if (ROPE) {
+            float ye, yo_;
+            f2_unpack(yw, ye, yo_);
             float e, o;
-            f2_unpack(f2_add(f2_mul(f2_pack(ye, yo_), f2_pack(cc[p], cc[p])),
+            f2_unpack(f2_add(f2_mul(yw, f2_pack(cc[p], cc[p])),
                              f2_mul(f2_pack(yo_, ye), f2_pack(-ss[p], ss[p]))),
                       e, o);
             y2[p] = __floats2bfloat162_rn(e, o);
           } else {
+            float ye, yo_;
+            f2_unpack(yw, ye, yo_);
             y2[p] = __floats2bfloat162_rn(ye, yo_);
           }
         }
@@ -377,7 +388,7 @@ __global__ void __launch_bounds__(256, kRowBlocksPerSM) rms_rope_kernel(
       }
     }
   };
-  row_pipeline<NV>(rows, load, body);
+  row_pipeline_f<NV, NV>(rows, load, prep, body);
 }
 
 static inline unsigned row_grid(int64_t rows, int blocks_per_sm = kRowBlocksPerSM) {
@@ -550,7 +561,7 @@ int fvb_rms_rope(const void* x, int64_t x_ld, const void* w, const float* cos, c
   const int hd = rope ? (int)head_dim : (head_dim > 0 ? (int)head_dim : 128);
   auto launch = [&](auto r, auto nv) {
     rms_rope_kernel<decltype(r)::value, decltype(nv)::value>
-        <<<row_grid(rows), 256, 0, (cudaStream_t)stream>>>(
+        <<<row_grid(rows, 2), 256, 0, (cudaStream_t)stream>>>(
             (const __nv_bfloat16*)x, x_ld, (const __nv_bfloat16*)w, rope ? cos : nullptr,
             rope ? sin : nullptr, rows, L, (int)D, hd, eps, out_row_map, (__nv_bfloat16*)out);
   };

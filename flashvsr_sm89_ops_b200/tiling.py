@@ -225,7 +225,8 @@ class _TileLoader:
 
 
 def render_tiled(pipe, lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
-                 tile_threshold=TILE_THRESHOLD, device=None, group=None, **pipe_kwargs):
+                 tile_threshold=TILE_THRESHOLD, device=None, group=None, timings=None,
+                 **pipe_kwargs):
     """Render lq_video [C,F,H,W] (or [1,C,F,H,W], in [-1, 1]) through `pipe` one tile at a time.
 
     Same contract as tiling.py:164-205: per-tile LQ crop, height/width and an
@@ -233,7 +234,15 @@ def render_tiled(pipe, lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
     runs on `device` (default: this rank's CUDA device, else CPU).  With a
     process group of N ranks each rank renders tiles i % N == rank and rank 0
     returns the reduced canvas (other ranks return None).
+
+    timings (optional dict, CUDA devices): filled with "events" (CUDA events at the start,
+    after this rank's last tile is blended, and after the cross-rank reduce), "load_wait_s"
+    (host seconds spent waiting for the next crop to be packed) and "tiles" (this rank's
+    tile count), so a caller can split the render into tile work, crop loading and the
+    exchange.
     """
+    import time
+
     import torch.distributed as dist
 
     batched = lq_video.dim() == 5
@@ -252,11 +261,18 @@ def render_tiled(pipe, lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
     mine = assign_tiles(len(tiles), world, rank)
     canvas = None
     n_out = torch.zeros(1, dtype=torch.int64, device=device)
+    events = None
+    if timings is not None and torch.device(device).type == "cuda":
+        events = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        events[0].record(torch.cuda.current_stream(device))
+    wait = 0.0
     loader = _TileLoader(lq, tiles, mine, device)
     try:
         for k, i in enumerate(mine):
             x, y, w, h = tiles[i]
+            t0 = time.perf_counter()
             crop = loader.get(k)
+            wait += time.perf_counter() - t0
             extra = {"topk_ratio": base_topk * (W * H) / (w * h)} if base_topk is not None else {}
             frames = pipe(LQ_video=crop.unsqueeze(0) if batched else crop, num_frames=num_frames,
                           height=h, width=w, **extra, **pipe_kwargs)
@@ -271,7 +287,13 @@ def render_tiled(pipe, lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
             del frames, crop
     finally:
         loader.close()
+    if events is not None:
+        events[1].record(torch.cuda.current_stream(device))
+    if timings is not None:
+        timings.update(events=events, load_wait_s=wait, tiles=len(mine))
     if world == 1:
+        if events is not None:
+            events[2].record(torch.cuda.current_stream(device))
         return canvas.to(dtype=lq_video.dtype)
     # every rank needs the output frame count to size its (possibly empty) canvas
     dist.all_reduce(n_out, op=dist.ReduceOp.MAX, group=group)
@@ -280,6 +302,8 @@ def render_tiled(pipe, lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
     elif canvas.shape[1] != int(n_out.item()):
         raise RuntimeError(f"rank {rank}: tile frame count {canvas.shape[1]} != {int(n_out.item())}")
     dist.reduce(canvas, dst=0, op=dist.ReduceOp.SUM, group=group)
+    if events is not None:
+        events[2].record(torch.cuda.current_stream(device))
     if rank == 0:
         return canvas.to(dtype=lq_video.dtype)
     return None
