@@ -48,6 +48,8 @@ _SIGS = {
     "fvb_quant_fp8_with_amax": (_int, [_vp, _i64, _i64, _vp, _int, _vp, _vp, _vp]),
     "fvb_fp8_ffn_workspace_bytes": (_sz, [_i64, _i64]),
     "fvb_fp8_ffn": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "fvb_fp8_ffn_residual": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64,
+                                    _i64, _vp, _vp, _vp, _vp, _vp]),
     "fvb_rms_rope": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _int, _vp, _vp, _vp]),
     "fvb_ln_modulate": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp, _vp, _vp]),
     "fvb_layer_norm": (_int, [_vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp, _vp]),
@@ -115,7 +117,7 @@ def _kernels_per_call(name: str, args) -> int:
     """How many of this library's kernels one C-ABI call launches."""
     if name in ("fvb_quant_fp8", "fvb_gelu_quant_fp8"):
         return 2 if args[5] == FVB_SCALE_TENSOR else 1
-    if name == "fvb_fp8_ffn":
+    if name in ("fvb_fp8_ffn", "fvb_fp8_ffn_residual"):
         return 3
     if name == "fvb_draft_block_mask":
         return 4

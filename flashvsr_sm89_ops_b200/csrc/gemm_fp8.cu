@@ -43,6 +43,10 @@ struct Cfg {
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
 };
 
+// epilogue of the FFN down-projection with the DiT block's gated residual add fused in:
+//   out = bf16(res + bf16(gate * bf16(acc * sa * sw + bias)))   (== fvb_gate_add of the GEMM)
+constexpr int kEpiGateResidual = 2;
+
 struct Args {
   int M, N, K;
   const float* sa;
@@ -52,6 +56,8 @@ struct Args {
   __nv_bfloat16* out;
   int64_t ldo;
   float* amax_out;
+  const __nv_bfloat16* res;   // kEpiGateResidual: residual [M, N] (row pitch ldo)
+  const __nv_bfloat16* gate;  // kEpiGateResidual: gate [N], or NULL for a plain add
 };
 
 constexpr int kStageBytes = 32 * 128;  // one epilogue warp's 32 rows x 64 bf16 columns
@@ -295,6 +301,25 @@ __global__ void __launch_bounds__(Cfg<EPI>::kThreads, 1)
               for (int i = 0; i < 8; ++i)
                 v[i] = __fmaf_rn(__uint_as_float(r[g4 * 8 + i]), sa * swv[i], bv[i]);
               packed = f32_to_bf16x8(v);
+              if (EPI == kEpiGateResidual) {
+                // bf16(res + bf16(g * y)): packed _rn forms round the exact product and the
+                // exact sum once, which is the eager bf16 chain bit for bit
+                uint4 ru = make_uint4(0u, 0u, 0u, 0u);
+                if (row_ok && cg < args.N)
+                  ru = __ldg(reinterpret_cast<const uint4*>(args.res + (int64_t)row * args.ldo + cg));
+                const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&ru);
+                __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&packed);
+                if (args.gate) {
+                  const uint4 gu = cg < args.N ? __ldg(reinterpret_cast<const uint4*>(args.gate + cg))
+                                               : make_uint4(0u, 0u, 0u, 0u);
+                  const __nv_bfloat162* gg = reinterpret_cast<const __nv_bfloat162*>(&gu);
+#pragma unroll
+                  for (int p = 0; p < 4; ++p) y2[p] = __hadd2_rn(r2[p], __hmul2_rn(gg[p], y2[p]));
+                } else {
+#pragma unroll
+                  for (int p = 0; p < 4; ++p) y2[p] = __hadd2_rn(r2[p], y2[p]);
+                }
+              }
             }
             // 128-byte swizzle: 16-byte chunk g of row `lane` lands at chunk g ^ (lane & 7)
             *reinterpret_cast<uint4*>(stg + lane * 128 + ((g ^ (lane & 7)) << 4)) = packed;
@@ -414,11 +439,47 @@ int fvb_fp8_gemm(const void* A, const float* sa, int a_mode, const void* W, cons
   a.amax_out = amax_out;
   const int bn = gemm::pick_bn(a.M, a.N);
   cudaStream_t st = (cudaStream_t)stream;
+  a.res = nullptr;
+  a.gate = nullptr;
   if (epilogue == FVB_EPI_NONE)
     return bn == 128 ? gemm::launch<128, FVB_EPI_NONE>(a, A, W, st)
                      : gemm::launch<256, FVB_EPI_NONE>(a, A, W, st);
   return bn == 128 ? gemm::launch<128, FVB_EPI_GELU_AMAX>(a, A, W, st)
                    : gemm::launch<256, FVB_EPI_GELU_AMAX>(a, A, W, st);
+}
+
+// FFN down-projection with the gated residual epilogue (fvb_fp8_ffn_residual's GEMM-2)
+static int fp8_gemm_gate_residual(const void* A, const float* sa, int a_mode, const void* W,
+                                  const float* sw, int w_mode, const void* bias, int64_t M,
+                                  int64_t N, int64_t K, const void* res, const void* gate,
+                                  void* out, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(M >= 0 && N > 0 && K > 0 && K % 16 == 0 && N % 8 == 0 && M < (1ll << 31) &&
+                  N < (1ll << 31) && K < (1ll << 31),
+              "fvb_fp8_ffn_residual: shape");
+  if (M == 0) return FVB_OK;
+  FVB_REQUIRE(A && W && sa && sw && out && res, "fvb_fp8_ffn_residual: NULL pointer");
+  FVB_REQUIRE(aligned16(A) && aligned16(W) && aligned16(out) && aligned16(res) &&
+                  (!bias || aligned16(bias)) && (!gate || aligned16(gate)),
+              "fvb_fp8_ffn_residual: pointers must be 16-byte aligned");
+  FVB_REQUIRE(w_mode != FVB_SCALE_ROW || aligned16(sw), "fvb_fp8_ffn_residual: sw alignment");
+  gemm::Args a;
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.sa = sa;
+  a.sw = sw;
+  a.a_row = a_mode == FVB_SCALE_ROW;
+  a.w_row = w_mode == FVB_SCALE_ROW;
+  a.bias = (const __nv_bfloat16*)bias;
+  a.out = (__nv_bfloat16*)out;
+  a.ldo = N;
+  a.amax_out = nullptr;
+  a.res = (const __nv_bfloat16*)res;
+  a.gate = (const __nv_bfloat16*)gate;
+  cudaStream_t st = (cudaStream_t)stream;
+  return gemm::pick_bn(a.M, a.N) == 128 ? gemm::launch<128, gemm::kEpiGateResidual>(a, A, W, st)
+                                        : gemm::launch<256, gemm::kEpiGateResidual>(a, A, W, st);
 }
 
 size_t fvb_fp8_ffn_workspace_bytes(int64_t M, int64_t F) {
@@ -427,10 +488,10 @@ size_t fvb_fp8_ffn_workspace_bytes(int64_t M, int64_t F) {
   return up((size_t)M * F * 2) + up((size_t)M * F) + up((size_t)(M > 0 ? M : 1) * 4) * 2;
 }
 
-int fvb_fp8_ffn(const void* x8, const float* sx, int mode, const void* W0, const float* sw0,
-                const void* b0, const void* W2, const float* sw2, const void* b2, int w_mode,
-                int64_t M, int64_t D, int64_t F, void* out, void* workspace,
-                fvb_stream_t stream) {
+static int ffn_impl(const void* x8, const float* sx, int mode, const void* W0, const float* sw0,
+                    const void* b0, const void* W2, const float* sw2, const void* b2, int w_mode,
+                    int64_t M, int64_t D, int64_t F, const void* res, const void* gate, void* out,
+                    void* workspace, fvb_stream_t stream) {
   using namespace fvb;
   FVB_REQUIRE(M >= 0 && D > 0 && F > 0, "fvb_fp8_ffn: shape");
   if (M == 0) return FVB_OK;
@@ -450,8 +511,30 @@ int fvb_fp8_ffn(const void* x8, const float* sx, int mode, const void* W0, const
   if (rc) return rc;
   rc = fvb_quant_fp8_with_amax(h, M, F, amax, mode, h8, hs, stream);
   if (rc) return rc;
+  if (res)
+    return fp8_gemm_gate_residual(h8, hs, mode, W2, sw2, w_mode, b2, M, D, F, res, gate, out,
+                                  stream);
   return fvb_fp8_gemm(h8, hs, mode, W2, sw2, w_mode, b2, M, D, F, out, FVB_EPI_NONE, nullptr,
                       stream);
+}
+
+int fvb_fp8_ffn(const void* x8, const float* sx, int mode, const void* W0, const float* sw0,
+                const void* b0, const void* W2, const float* sw2, const void* b2, int w_mode,
+                int64_t M, int64_t D, int64_t F, void* out, void* workspace,
+                fvb_stream_t stream) {
+  return ffn_impl(x8, sx, mode, W0, sw0, b0, W2, sw2, b2, w_mode, M, D, F, nullptr, nullptr, out,
+                  workspace, stream);
+}
+
+int fvb_fp8_ffn_residual(const void* x8, const float* sx, int mode, const void* W0,
+                         const float* sw0, const void* b0, const void* W2, const float* sw2,
+                         const void* b2, int w_mode, int64_t M, int64_t D, int64_t F,
+                         const void* residual, const void* gate, void* out, void* workspace,
+                         fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(residual != nullptr, "fvb_fp8_ffn_residual: residual is NULL");
+  return ffn_impl(x8, sx, mode, W0, sw0, b0, W2, sw2, b2, w_mode, M, D, F, residual, gate, out,
+                  workspace, stream);
 }
 
 }  // extern "C"

@@ -35,13 +35,13 @@ __device__ __forceinline__ uint2 fp8_codes8(const uint4& y, float qs, float rqs)
 // Gated residual add of one row held in registers (the gate_add_kernel arithmetic):
 // x <- bf16(x + bf16(g * r)) (g == nullptr: bf16(x + r)), also stored to xo; raw holds
 // the row's x vectors then its r vectors.
-template <int NV>
+template <int NV, bool FULL>
 __device__ __forceinline__ void gate_add_row(const uint4* raw, uint4* xr, int lane, int nvec,
                                              const __nv_bfloat16* g, uint4* xo) {
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int v = j * 32 + lane;
-    if (v < nvec) {
+    if (FULL || v < nvec) {
       float xf[8], rf[8];
       bf16x8_to_f32(raw[j], xf);
       bf16x8_to_f32(raw[NV + j], rf);
@@ -61,14 +61,15 @@ __device__ __forceinline__ void gate_add_row(const uint4* raw, uint4* xr, int la
 }
 
 // Row mean and (x - mean) * rden with rden = 1/sqrt(var + eps), two-pass in registers.
-// x holds NV 16-byte vectors per lane (bf16); sums use packed fp32 pairs.
-template <int NV>
+// x holds NV 16-byte vectors per lane (bf16); sums use packed fp32 pairs.  FULL: the row
+// fills every lane's NV vectors (D == 256 * NV), so no per-vector bounds test is needed.
+template <int NV, bool FULL>
 __device__ __forceinline__ void row_stats(const uint4* xr, int lane, int nvec, int D, float eps,
                                           float& mean, float& rden) {
   uint64_t s2 = f2_pack(0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    if (j * 32 + lane < nvec) {
+    if ((FULL || j * 32 + lane < nvec)) {
       float f[8];
       bf16x8_to_f32(xr[j], f);
 #pragma unroll
@@ -77,12 +78,12 @@ __device__ __forceinline__ void row_stats(const uint4* xr, int lane, int nvec, i
   }
   float sa, sb;
   f2_unpack(s2, sa, sb);
-  mean = __fdiv_rn(warp_sum(sa + sb), (float)D);
+  mean = warp_sum(sa + sb) * (1.0f / (float)D);
   const uint64_t nm = f2_pack(-mean, -mean);
   uint64_t q2 = f2_pack(0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    if (j * 32 + lane < nvec) {
+    if ((FULL || j * 32 + lane < nvec)) {
       float f[8];
       bf16x8_to_f32(xr[j], f);
 #pragma unroll
@@ -94,9 +95,10 @@ __device__ __forceinline__ void row_stats(const uint4* xr, int lane, int nvec, i
   }
   float qa, qb;
   f2_unpack(q2, qa, qb);
-  // (x - mean) / sqrt(var + eps) as a product with the correctly rounded reciprocal square
-  // root: at most one fp32 ulp from the quotient, well inside the bf16 rounding that follows
-  rden = __frsqrt_rn(__fdiv_rn(warp_sum(qa + qb), (float)D) + eps);
+  // mean = sum * (1/D), var = sumsq * (1/D) and the approximate reciprocal square root: each
+  // within an fp32 ulp or two of the reference's sum / D and 1 / sqrt(.) (which its Triton
+  // kernel also evaluates approximately), far inside the bf16 rounding that follows
+  rden = rsqrtf(warp_sum(qa + qb) * (1.0f / (float)D) + eps);
 }
 
 // LayerNorm + AdaLN modulate.  The modulate chain is bf16 arithmetic on bf16 operands:
@@ -107,7 +109,7 @@ __device__ __forceinline__ void row_stats(const uint4* xr, int lane, int nvec, i
 // GATE: the row is first the gated residual sum x + g * r of gate_add_kernel (stored to
 // x_out), so the add and the norm that follows it read the residual stream once.  out may
 // be nullptr when only the FP8 codes are consumed.
-template <bool EMIT_FP8, int NV, bool GATE>
+template <bool EMIT_FP8, int NV, bool GATE, bool FULL>
 __global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ gate,
     const __nv_bfloat16* __restrict__ r, __nv_bfloat16* __restrict__ x_out,
@@ -120,12 +122,12 @@ __global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_k
     const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
 #pragma unroll
     for (int j = 0; j < NV; ++j)
-      if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+      if ((FULL || j * 32 + lane < nvec)) xr[j] = __ldg(xv + j * 32 + lane);
     if (GATE) {
       const uint4* rv = reinterpret_cast<const uint4*>(r + row * D);
 #pragma unroll
       for (int j = 0; j < NV; ++j)
-        if (j * 32 + lane < nvec) xr[NV + j] = __ldg(rv + j * 32 + lane);
+        if ((FULL || j * 32 + lane < nvec)) xr[NV + j] = __ldg(rv + j * 32 + lane);
     }
   };
   auto body = [&](int64_t row, uint4* xr) {
@@ -134,7 +136,7 @@ __global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_k
     const uint4* sv = reinterpret_cast<const uint4*>(scale + b * D);
     const uint4* hv = reinterpret_cast<const uint4*>(shift + b * D);
     float mean, rden;
-    row_stats<NV>(xr, lane, nvec, D, eps, mean, rden);
+    row_stats<NV, FULL>(xr, lane, nvec, D, eps, mean, rden);
     const uint64_t nm = f2_pack(-mean, -mean), rd = f2_pack(rden, rden);
     const __nv_bfloat162 one2 = __float2bfloat162_rn(1.0f);
     __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
@@ -142,7 +144,7 @@ __global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_k
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int v = j * 32 + lane;
-      if (v < nvec) {
+      if (FULL || v < nvec) {
         float f[8];
         bf16x8_to_f32(xr[j], f);
         const uint4 su = __ldg(sv + v), hu = __ldg(hv + v);
@@ -173,14 +175,14 @@ __global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_k
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
         const int v = j * 32 + lane;
-        if (v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
+        if (FULL || v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
       }
       if (lane == 0) q_scale[row] = returned_scale(amax);
     }
   };
   if (GATE) {
     auto prep = [&](int64_t row, const uint4* raw, uint4* xr) {
-      gate_add_row<NV>(raw, xr, lane, nvec, gate ? gate + (row / L) * D : nullptr,
+      gate_add_row<NV, FULL>(raw, xr, lane, nvec, gate ? gate + (row / L) * D : nullptr,
                        reinterpret_cast<uint4*>(x_out + row * D));
     };
     row_pipeline_prep<NV, 2 * NV>(rows, load, prep, body);
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_k
 // (what the next FP8 linear would compute from it).
 // GATE: as for ln_modulate_kernel, the row is first x + g * r (stored to x_out; the gate
 // row of batch item row / L).
-template <bool EMIT_FP8, int NV, bool GATE>
+template <bool EMIT_FP8, int NV, bool GATE, bool FULL>
 __global__ void __launch_bounds__(256, 2) layer_norm_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ gate,
     const __nv_bfloat16* __restrict__ r, __nv_bfloat16* __restrict__ x_out, int64_t L,
@@ -208,24 +210,24 @@ __global__ void __launch_bounds__(256, 2) layer_norm_kernel(
     const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
 #pragma unroll
     for (int j = 0; j < NV; ++j)
-      if (j * 32 + lane < nvec) xr[j] = __ldg(xv + j * 32 + lane);
+      if ((FULL || j * 32 + lane < nvec)) xr[j] = __ldg(xv + j * 32 + lane);
     if (GATE) {
       const uint4* rv = reinterpret_cast<const uint4*>(r + row * D);
 #pragma unroll
       for (int j = 0; j < NV; ++j)
-        if (j * 32 + lane < nvec) xr[NV + j] = __ldg(rv + j * 32 + lane);
+        if ((FULL || j * 32 + lane < nvec)) xr[NV + j] = __ldg(rv + j * 32 + lane);
     }
   };
   auto body = [&](int64_t row, uint4* xr) {
     float mean, rstd;
-    row_stats<NV>(xr, lane, nvec, D, eps, mean, rstd);
+    row_stats<NV, FULL>(xr, lane, nvec, D, eps, mean, rstd);
     const uint64_t nm = f2_pack(-mean, -mean), rs2 = f2_pack(rstd, rstd);
     __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
     uint4* ov = reinterpret_cast<uint4*>(out + row * D);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int v = j * 32 + lane;
-      if (v < nvec) {
+      if (FULL || v < nvec) {
         float f[8], ww[8], bb[8];
         bf16x8_to_f32(xr[j], f);
         if (w) bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), ww);
@@ -260,14 +262,14 @@ __global__ void __launch_bounds__(256, 2) layer_norm_kernel(
 #pragma unroll
       for (int j = 0; j < NV; ++j) {
         const int v = j * 32 + lane;
-        if (v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
+        if (FULL || v < nvec) qv[v] = fp8_codes8(xr[j], qs, rqs);
       }
       if (lane == 0) q_scale[row] = returned_scale(amax);
     }
   };
   if (GATE) {
     auto prep = [&](int64_t row, const uint4* raw, uint4* xr) {
-      gate_add_row<NV>(raw, xr, lane, nvec, gate ? gate + (row / L) * D : nullptr,
+      gate_add_row<NV, FULL>(raw, xr, lane, nvec, gate ? gate + (row / L) * D : nullptr,
                        reinterpret_cast<uint4*>(x_out + row * D));
     };
     row_pipeline_prep<NV, 2 * NV>(rows, load, prep, body);
@@ -418,11 +420,17 @@ static int ln_modulate_impl(const void* x, const void* gate, const void* r, void
               "%s: pointers must be 16-byte aligned", name);
   if (q8) FVB_REQUIRE((reinterpret_cast<uintptr_t>(q8) & 7u) == 0, "%s: q8 alignment", name);
   auto launch = [&](auto emit, auto nv, auto gated) {
-    ln_modulate_kernel<decltype(emit)::value, decltype(nv)::value, decltype(gated)::value>
-        <<<row_grid(rows, gated ? 2 : kRowBlocksPerSM), 256, 0, (cudaStream_t)stream>>>(
-            (const __nv_bfloat16*)x, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)r,
-            (__nv_bfloat16*)x_out, (const __nv_bfloat16*)scale, (const __nv_bfloat16*)shift, rows,
-            L, (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
+    constexpr int NV = decltype(nv)::value;
+    auto go = [&](auto full) {
+      ln_modulate_kernel<decltype(emit)::value, NV, decltype(gated)::value, decltype(full)::value>
+          <<<row_grid(rows, gated ? 2 : kRowBlocksPerSM), 256, 0, (cudaStream_t)stream>>>(
+              (const __nv_bfloat16*)x, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)r,
+              (__nv_bfloat16*)x_out, (const __nv_bfloat16*)scale, (const __nv_bfloat16*)shift,
+              rows, L, (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
+    };
+    // (the plain bf16-output form spills in its FULL build at this register budget)
+    if (D == NV * 256 && (decltype(emit)::value || decltype(gated)::value)) go(std::true_type{});
+    else go(std::false_type{});
   };
   dispatch_nv(D, [&](auto nv) {
     if (r) {
@@ -446,11 +454,16 @@ static int layer_norm_impl(const void* x, const void* gate, const void* r, void*
               "%s: pointers must be 16-byte aligned", name);
   if (q8) FVB_REQUIRE((reinterpret_cast<uintptr_t>(q8) & 7u) == 0, "%s: q8 alignment", name);
   auto launch = [&](auto emit, auto nv, auto gated) {
-    layer_norm_kernel<decltype(emit)::value, decltype(nv)::value, decltype(gated)::value>
-        <<<row_grid(rows, 2), 256, 0, (cudaStream_t)stream>>>(
-            (const __nv_bfloat16*)x, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)r,
-            (__nv_bfloat16*)x_out, L, (const __nv_bfloat16*)w, (const __nv_bfloat16*)b, rows,
-            (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
+    constexpr int NV = decltype(nv)::value;
+    auto go = [&](auto full) {
+      layer_norm_kernel<decltype(emit)::value, NV, decltype(gated)::value, decltype(full)::value>
+          <<<row_grid(rows, 2), 256, 0, (cudaStream_t)stream>>>(
+              (const __nv_bfloat16*)x, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)r,
+              (__nv_bfloat16*)x_out, L, (const __nv_bfloat16*)w, (const __nv_bfloat16*)b, rows,
+              (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
+    };
+    if (D == NV * 256) go(std::true_type{});
+    else go(std::false_type{});
   };
   dispatch_nv(D, [&](auto nv) {
     if (r) {

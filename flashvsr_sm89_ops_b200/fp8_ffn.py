@@ -18,8 +18,14 @@ from .fp8_linear import FP8Linear
 from .fp8_quant import fused_gelu_quant_fp8, mode_code, quantize_fp8  # noqa: F401 (re-export)
 
 
-def ffn_fp8(x8, sx, lin0: FP8Linear, lin2: FP8Linear, out=None, workspace=None):
-    """Pre-quantised input -> FFN output through fvb_fp8_ffn (one C-ABI call)."""
+def ffn_fp8(x8, sx, lin0: FP8Linear, lin2: FP8Linear, out=None, workspace=None,
+            residual=None, gate=None):
+    """Pre-quantised input -> FFN output through fvb_fp8_ffn (one C-ABI call).
+
+    residual ([M, D] bf16, with gate [D] bf16 or None): return the DiT block's gated
+    residual update bf16(residual + bf16(gate * FFN(x))) instead (fvb_fp8_ffn_residual: the
+    add runs in the down-projection's epilogue), bit for bit fused_gate_add(residual, gate,
+    FFN(x))."""
     M, D = x8.shape
     F = lin0.weight.shape[0]
     if lin0.mode != lin2.mode:
@@ -33,6 +39,18 @@ def ffn_fp8(x8, sx, lin0: FP8Linear, lin2: FP8Linear, out=None, workspace=None):
     a_code = _lib.FVB_SCALE_ROW if (sx.numel() == M and M > 1) else _lib.FVB_SCALE_TENSOR
     if a_code != code and M > 1:
         raise ValueError("FP8FFN: activation scale granularity does not match the module")
+    if residual is not None:
+        residual = residual.reshape(M, -1)
+        if residual.dtype != torch.bfloat16 or not residual.is_contiguous():
+            raise ValueError("ffn_fp8: residual must be a contiguous bf16 [M, D] tensor")
+        if gate is not None:
+            gate = gate.reshape(-1).contiguous()
+        _lib.call("fvb_fp8_ffn_residual", _lib.ptr(x8), _lib.ptr(sx), a_code,
+                  _lib.ptr(lin0.weight), _lib.ptr(lin0.w_scale), _lib.ptr(lin0.bias),
+                  _lib.ptr(lin2.weight), _lib.ptr(lin2.w_scale), _lib.ptr(lin2.bias), code, M, D,
+                  F, _lib.ptr(residual), _lib.ptr(gate), _lib.ptr(out), _lib.ptr(workspace),
+                  _lib.stream_of(x8))
+        return out
     _lib.call("fvb_fp8_ffn", _lib.ptr(x8), _lib.ptr(sx), a_code, _lib.ptr(lin0.weight),
               _lib.ptr(lin0.w_scale), _lib.ptr(lin0.bias), _lib.ptr(lin2.weight),
               _lib.ptr(lin2.w_scale), _lib.ptr(lin2.bias), code, M, D, F, _lib.ptr(out),

@@ -405,13 +405,18 @@ def _make_dit_block_forward(dit):
                 x, _, x8, s8 = gate_add_ln_modulate(x, None, ca_out, scale_mlp, shift_mlp,
                                                     eps=_module_eps(self.norm2), emit_fp8=True,
                                                     want_out=False)
-                y = ffn_fp8(x8.view(-1, x.shape[-1]), s8, ffn.lin0, ffn.lin2).view(x.shape)
+                # FFN and the block's closing gated residual add in one call (the add runs in
+                # the down-projection's epilogue; bit for bit gate_add(x, gate_mlp, FFN(.)))
+                x = ffn_fp8(x8.view(-1, x.shape[-1]), s8, ffn.lin0, ffn.lin2, residual=x,
+                            gate=gate_mlp).view(x.shape)
+                y = None
             else:
                 if ca_out is not None:
                     x = fused_gate_add(x, None, ca_out)
                 input_x = ln_mod(x, scale_mlp, shift_mlp, eps=_module_eps(self.norm2))
                 y = self.ffn(input_x)
-            x = gate_add(x, gate_mlp, y)
+            if y is not None:
+                x = gate_add(x, gate_mlp, y)
         else:
             input_x = dit.modulate(self.norm2(x), shift_mlp, scale_mlp)
             x = self.gate(x, gate_mlp, self.ffn(input_x))

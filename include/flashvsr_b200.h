@@ -125,6 +125,17 @@ FVB_API int fvb_fp8_ffn(const void* x8, const float* sx, int mode, const void* W
                 const void* b0, const void* W2, const float* sw2, const void* b2, int w_mode,
                 int64_t M, int64_t D, int64_t F, void* out, void* workspace, fvb_stream_t stream);
 
+/* The FFN and the DiT block's gated residual add after it in one call (the block's
+ * x = fused_gate_add(x, gate_mlp, FP8FFN(.)), integrate.py:178-179 with fused_adaln.py:74-85):
+ *   out = bf16(residual + bf16(gate * FFN(x8)))  bit for bit (gate == NULL: plain add),
+ * the add applied in the down-projection's epilogue, so the FFN output is never stored and
+ * re-read.  residual / out [M, D] bf16 (out may be residual itself), gate [D] bf16. */
+FVB_API int fvb_fp8_ffn_residual(const void* x8, const float* sx, int mode, const void* W0,
+                                 const float* sw0, const void* b0, const void* W2,
+                                 const float* sw2, const void* b2, int w_mode, int64_t M,
+                                 int64_t D, int64_t F, const void* residual, const void* gate,
+                                 void* out, void* workspace, fvb_stream_t stream);
+
 /* ------------------------------------------------- a7: RMSNorm + 3-D RoPE
  * Replaces fused_rms_rope(x, weight, freqs_cis, eps, rope, head_dim)
  * (fused_rms_rope.py:66-83; kernel :21-55):

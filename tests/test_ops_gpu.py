@@ -437,6 +437,33 @@ def test_fp8_ffn(mode):
     assert max_rel(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("mode", ["tensor", "token"])
+@pytest.mark.parametrize("gated", [True, False])
+def test_fp8_ffn_residual_equals_ffn_then_gate_add(mode, gated):
+    """fvb_fp8_ffn_residual (the gated residual add in the down-projection's epilogue) is bit
+    for bit fused_gate_add(x, gate, FFN(x_in)) -- the DiT block's closing update."""
+    from flashvsr_sm89_ops_b200 import fused_gate_add, quantize_fp8
+    from flashvsr_sm89_ops_b200.fp8_ffn import ffn_fp8
+    from flashvsr_sm89_ops_b200.fp8_linear import FP8Linear
+    D, Fh, M = 1536, 8960, 1000
+    g = gen(33)
+    l0 = torch.nn.Linear(D, Fh).to(torch.bfloat16)
+    l2 = torch.nn.Linear(Fh, D).to(torch.bfloat16)
+    with torch.no_grad():
+        for lin in (l0, l2):
+            lin.weight.copy_(torch.randn(lin.weight.shape, generator=g) * 0.02)
+            lin.bias.copy_(torch.randn(lin.bias.shape, generator=g) * 0.02)
+    f0, f2 = FP8Linear(l0.to(DEV), mode), FP8Linear(l2.to(DEV), mode)
+    xin = torch.randn(M, D, generator=g).to(torch.bfloat16).to(DEV)
+    res = (torch.randn(1, M, D, generator=g) * 3).to(torch.bfloat16).to(DEV)
+    gate = torch.randn(1, 1, D, generator=g).to(torch.bfloat16).to(DEV) if gated else None
+    x8, sx = quantize_fp8(xin, mode)
+    y = ffn_fp8(x8, sx, f0, f2)
+    ref = fused_gate_add(res, gate, y.view(1, M, D))
+    got = ffn_fp8(x8, sx, f0, f2, residual=res, gate=gate)
+    assert torch.equal(got.view(1, M, D), ref)
+
+
 # ----------------------------------------------------------------------------- attention
 ATTN_CASES = [(16, 24, 0, 0.4), (32, 48, 0, 0.3), (48, 88, 198, 0.46)]  # lcsa/test_correctness.py:46-50
 
