@@ -367,11 +367,14 @@ def tiled_4k(runner, world, rank, dev, dist_mod):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stream = torch.cuda.current_stream(dev)
     tm = {}
+    sampler = ClockSampler(dev.index if dev.index is not None else 0)
+    sampler.start()
     e0.record(stream)
     out = render_tiled(pipe, lq, tile_target=700_000, tile_threshold=700_000, device=dev,
                        timings=tm)
     e1.record(stream)
     torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
     ev = tm["events"]
     # this rank's split: its tiles (render + blend), the cross-rank reduce, crop-packing waits
     part = torch.tensor([ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), tm["load_wait_s"] * 1e3,
@@ -394,12 +397,14 @@ def tiled_4k(runner, world, rank, dev, dist_mod):
         if rank == 0:
             pipe.tokens = 0
             s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            solo_sampler = ClockSampler(dev.index if dev.index is not None else 0)
+            solo_sampler.start()
             s0.record(stream)
             ref = render_tiled(pipe, lq, tile_target=700_000, tile_threshold=700_000, device=dev,
                                group=g0)
             s1.record(stream)
             torch.cuda.synchronize(dev)
-            solo = {"ms": s0.elapsed_time(s1),
+            solo = {"ms": s0.elapsed_time(s1), "clocks": solo_sampler.stop(),
                     "max_abs_diff_vs_sharded": float((ref.float() - out.float()).abs().max().item())}
             del ref
         dist_mod.barrier()
@@ -417,6 +422,7 @@ def tiled_4k(runner, world, rank, dev, dist_mod):
     extra = {}
     if solo is not None:
         extra = {"n1_same_job_ms": solo["ms"], "n1_same_job_fps": n_out / (solo["ms"] / 1e3),
+                 "n1_same_job_clocks_rank0": solo["clocks"],
                  "efficiency_vs_n1_same_job": solo["ms"] / (world * ms),
                  "n1_max_abs_diff_vs_sharded": solo["max_abs_diff_vs_sharded"]}
     return {
@@ -428,7 +434,7 @@ def tiled_4k(runner, world, rank, dev, dist_mod):
         "schedule": "per tile: f=6 chunk + 7 f=2 chunks (KV cache of 3 time rows), 30 blocks; "
                     "patch-embed / unpatchify are bf16 linears standing in for the LQ "
                     "projection and VAE",
-        "breakdown": breakdown, **extra,
+        "breakdown": breakdown, "clocks_rank0": clocks, **extra,
     }
 
 

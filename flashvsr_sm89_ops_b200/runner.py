@@ -166,7 +166,7 @@ class TiledDiTPipe:
     [3, 4 * (6 + 2 * n_steps), h, w] bf16 frames.
     """
 
-    def __init__(self, runner: StreamingDiT, n_steps: int = 7, seed: int = 5):
+    def __init__(self, runner: StreamingDiT, n_steps: int = 7, seed: int = 5, graph: bool = True):
         self.r = runner
         self.n_steps = n_steps
         dev = runner.device
@@ -175,19 +175,54 @@ class TiledDiTPipe:
         self.emb = (0.02 * torch.randn(patch, runner.dim, generator=g, device=dev)).to(torch.bfloat16)
         self.unemb = (0.02 * torch.randn(runner.dim, patch, generator=g, device=dev)).to(torch.bfloat16)
         self.tokens = 0
+        # graph=True: a tile's whole schedule (patch-embed, every chunk through every block,
+        # unpatchify) is captured once per crop shape as one CUDA graph and replayed for each
+        # tile of that shape, so a tile costs one launch on the host instead of thousands.
+        # The returned frames then live in the graph's output buffer, valid until the next call.
+        self.graph = graph and torch.device(dev).type == "cuda"
+        self._graphs = {}
+        self._freqs = {}
 
     def latent_frames(self):
         return 6 + 2 * self.n_steps
 
     @torch.no_grad()
     def __call__(self, LQ_video, num_frames=None, height=None, width=None, **kwargs):
-        r = self.r
         crop = LQ_video[0] if LQ_video.dim() == 5 else LQ_video
         C, F, h, w = crop.shape
         lf = self.latent_frames()
         if C != 3 or F < 4 * lf + 1 or h % 16 or w % 16:
             raise ValueError(f"TiledDiTPipe: crop {tuple(crop.shape)} needs 3 channels, "
                              f">= {4 * lf + 1} frames and 16-px multiples")
+        tokens = lf * (h // 16) * (w // 16)
+        if not self.graph:
+            self.tokens += tokens
+            return self._forward(crop)
+        key = (tuple(crop.shape), crop.dtype)
+        st = self._graphs.get(key)
+        if st is None:
+            static_in = crop.clone()
+            self._forward(static_in)  # eager warm-up: lazy allocations and caches
+            side = torch.cuda.Stream(self.r.device)
+            side.wait_stream(torch.cuda.current_stream(self.r.device))
+            with torch.cuda.stream(side):
+                self._forward(static_in)
+            torch.cuda.current_stream(self.r.device).wait_stream(side)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                static_out = self._forward(static_in)
+            st = (gr, static_in, static_out)
+            self._graphs[key] = st
+        gr, static_in, static_out = st
+        static_in.copy_(crop)
+        gr.replay()
+        self.tokens += tokens
+        return static_out
+
+    def _forward(self, crop):
+        r = self.r
+        C, F, h, w = crop.shape
+        lf = self.latent_frames()
         hh, ww = h // 16, w // 16
         # [3, 4*lf, h, w] -> tokens [lf*hh*ww, 3*4*16*16] in (f, h, w) raster order
         v = crop[:, 1:1 + 4 * lf].to(torch.bfloat16)
@@ -200,11 +235,14 @@ class TiledDiTPipe:
         caches = None
         for f in [6] + [2] * self.n_steps:
             xc = x[:, f0 * per:(f0 + f) * per]
-            fr = dit.chunk_freqs(f, hh, ww, f0, r.device)
+            fkey = (f, hh, ww, f0)
+            fr = self._freqs.get(fkey)
+            if fr is None:  # built on the host once per chunk shape, before any capture
+                fr = dit.chunk_freqs(f, hh, ww, f0, r.device)
+                self._freqs[fkey] = fr
             y, caches = dit.forward_chunk(xc, r.t_mod, fr, (f, hh, ww), caches, topk=r.topk,
                                           kv_len=r.kv_len)
             outs.append(y[0])
-            self.tokens += y.shape[1]
             f0 += f
         p = torch.cat(outs) @ self.unemb  # [lf*hh*ww, 3*4*16*16]
         p = p.reshape(lf, hh, ww, C, 4, 16, 16).permute(3, 0, 4, 1, 5, 2, 6)
