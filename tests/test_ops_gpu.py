@@ -334,6 +334,37 @@ def test_fp8_gemm(M, N, K, mode):
     assert max_rel(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("epilogue", [0, 1])
+def test_fp8_gemm_cta_pair_rows_equal_single_cta(epilogue):
+    """Wide GEMMs (N >= 4096) with more than 128 rows run on CTA pairs (cta_group::2, 256-row
+    tiles: the even CTA's TMEM holds rows 0-127 of a tile, the odd CTA's rows 128-255).
+    Every row must be bit for bit what the single-CTA kernel (M <= 128) gives for that row
+    alone: rows 0-127 from the even CTA, 128-255 from the odd one, 256-299 from a pair whose
+    odd CTA has no valid row.  N = 4104 also leaves a ragged last column tile."""
+    from flashvsr_sm89_ops_b200 import _lib, quantize_fp8
+    from flashvsr_sm89_ops_b200.fp8_linear import fp8_mm, quantize_weight
+    M, N, K = 300, 4104, 1536
+    g = gen(77)
+    x = O.fp8_outlier_activations(M, K, g)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    qw, sw = quantize_weight(w.to(DEV), "token")
+    qx, sx = quantize_fp8(x.to(DEV), "token")
+
+    def run(lo, hi):
+        amax = torch.zeros(hi - lo, device=DEV)
+        kw = dict(epilogue=_lib.FVB_EPI_GELU_AMAX, amax_out=amax) if epilogue else {}
+        y = fp8_mm(qx[lo:hi].contiguous(), sx[lo:hi].contiguous(), qw, sw, b, **kw)
+        return y, amax
+
+    whole, amax_whole = run(0, M)
+    for lo, hi in ((0, 128), (128, 256), (256, M)):
+        part, amax_part = run(lo, hi)
+        assert torch.equal(whole[lo:hi], part), (lo, hi)
+        if epilogue:
+            assert torch.equal(amax_whole[lo:hi], amax_part), (lo, hi)
+
+
 # BASELINE configuration 2: every (K -> N) pair at the two large token counts.  The GEMM
 # runs in full on the GPU; the oracle (fp32 product of the decoded codes, CPU) checks two
 # rows of every 128-row tile (rows are independent, so a tile's rows share its code path).
