@@ -146,6 +146,71 @@ def _dist_info(group):
     return 1, 0
 
 
+class _Staging:
+    """Two pinned host buffers and two device buffers for one device and dtype, with the
+    events that order their reuse, kept across render_tiled calls: pinning a few hundred MB
+    of host memory takes a large fraction of a second, which a fresh allocation per call
+    would add to every render.  Calls on one device share them, so render_tiled calls on
+    the same device must not run concurrently from several host threads."""
+
+    def __init__(self, device, dtype, numel):
+        self.stage = [torch.empty(numel, dtype=dtype, pin_memory=True) for _ in range(2)]
+        self.dev = [torch.empty(numel, dtype=dtype, device=device) for _ in range(2)]
+        self.up_done = [None, None]    # upload from stage b finished (host may refill it)
+        self.used = [None, None]       # render of the tile in device buffer b finished
+
+    def numel(self):
+        return self.stage[0].numel()
+
+
+_STAGING = {}
+
+
+def _staging_for(device, dtype, numel):
+    key = (str(torch.device(device)), dtype)
+    st = _STAGING.get(key)
+    if st is None or st.numel() < numel:
+        if st is not None:  # the old buffers may still feed work in flight
+            for ev in st.up_done + st.used:
+                if ev is not None:
+                    ev.synchronize()
+        st = _Staging(device, dtype, numel)
+        _STAGING[key] = st
+    return st
+
+
+def _crop_numel(lq, tiles, order):
+    return max((tiles[i][2] * tiles[i][3] for i in order), default=0) * lq.shape[0] * lq.shape[1]
+
+
+def reserve_staging(lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
+                    tile_threshold=TILE_THRESHOLD, device=None, group=None):
+    """Allocate this rank's crop staging for render_tiled(lq_video, ...) ahead of the first
+    call (same tiling arguments), so that call does not pay for pinning host memory.  The
+    buffers stay allocated until release_staging()."""
+    lq = lq_video[0] if lq_video.dim() == 5 else lq_video
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    device = torch.device(device)
+    if lq.device == device or device.type != "cuda":
+        return
+    C, F, H, W = lq.shape
+    tiles = plan_tiles(W, H, target=tile_target, threshold=tile_threshold, overlap=overlap)
+    world, rank = _dist_info(group)
+    n = _crop_numel(lq, tiles, assign_tiles(len(tiles), world, rank))
+    if n:
+        _staging_for(device, lq.dtype, n)
+
+
+def release_staging():
+    """Free the crop staging buffers kept by render_tiled / reserve_staging."""
+    for st in _STAGING.values():
+        for ev in st.up_done + st.used:
+            if ev is not None:
+                ev.synchronize()
+    _STAGING.clear()
+
+
 class _TileLoader:
     """Brings the LQ crops of one rank's tiles onto its GPU ahead of use.
 
@@ -153,9 +218,9 @@ class _TileLoader:
     plus a synchronous pageable transfer per tile, in series with the tile's compute.  Here
     a worker thread packs crop k+1 into a pinned staging buffer while the GPU renders tile k,
     a side stream uploads it, and the render stream waits on an event.  Two staging and two
-    device buffers rotate; the side stream reuses a device buffer only after the render of
-    the tile that used it (an event recorded after its blend).  A video already on the
-    device is cropped there.
+    device buffers rotate (kept across calls, see _Staging); the side stream reuses a device
+    buffer only after the render of the tile that used it (an event recorded after its
+    blend).  A video already on the device is cropped there.
     """
 
     def __init__(self, lq, tiles, order, device):
@@ -165,13 +230,8 @@ class _TileLoader:
         if self.direct:
             return
         from concurrent.futures import ThreadPoolExecutor
-        C, F = lq.shape[0], lq.shape[1]
-        n = max((tiles[i][2] * tiles[i][3] for i in self.order), default=0) * C * F
-        self.stage = [torch.empty(n, dtype=lq.dtype, pin_memory=True) for _ in range(2)]
-        self.dev = [torch.empty(n, dtype=lq.dtype, device=device) for _ in range(2)]
+        self.st = _staging_for(device, lq.dtype, _crop_numel(lq, tiles, self.order))
         self.copy_stream = torch.cuda.Stream(device)
-        self.up_done = [None, None]    # upload of buffer b finished (host may refill stage b)
-        self.used = [None, None]       # render of the tile in device buffer b finished
         self.pool = ThreadPoolExecutor(1)
         self.pending = self.pool.submit(self._pack, 0) if self.order else None
 
@@ -182,11 +242,11 @@ class _TileLoader:
     def _pack(self, k):
         x, y, w, h = self.tiles[self.order[k]]
         b = k & 1
-        if self.up_done[b] is not None:
-            self.up_done[b].synchronize()  # stage b still feeds an upload in flight
+        if self.st.up_done[b] is not None:
+            self.st.up_done[b].synchronize()  # stage b still feeds an upload in flight
         shp = self._shape(k)
         n = shp[0] * shp[1] * shp[2] * shp[3]
-        self.stage[b][:n].view(shp).copy_(self.lq[:, :, y:y + h, x:x + w])
+        self.st.stage[b][:n].view(shp).copy_(self.lq[:, :, y:y + h, x:x + w])
         return k
 
     def get(self, k):
@@ -198,16 +258,17 @@ class _TileLoader:
         b = k & 1
         shp = self._shape(k)
         n = shp[0] * shp[1] * shp[2] * shp[3]
+        st = self.st
         with torch.cuda.stream(self.copy_stream):
-            if self.used[b] is not None:
-                self.copy_stream.wait_event(self.used[b])
-            self.dev[b][:n].copy_(self.stage[b][:n], non_blocking=True)
+            if st.used[b] is not None:
+                self.copy_stream.wait_event(st.used[b])
+            st.dev[b][:n].copy_(st.stage[b][:n], non_blocking=True)
             ev = torch.cuda.Event()
             ev.record(self.copy_stream)
-        self.up_done[b] = ev
+        st.up_done[b] = ev
         self.pending = self.pool.submit(self._pack, k + 1) if k + 1 < len(self.order) else None
         torch.cuda.current_stream(self.device).wait_event(ev)
-        return self.dev[b][:n].view(shp)
+        return st.dev[b][:n].view(shp)
 
     def done(self, k):
         """The render stream has finished with tile order[k]'s device buffer."""
@@ -215,7 +276,7 @@ class _TileLoader:
             return
         ev = torch.cuda.Event()
         ev.record(torch.cuda.current_stream(self.device))
-        self.used[k & 1] = ev
+        self.st.used[k & 1] = ev
 
     def close(self):
         if not self.direct:

@@ -51,3 +51,24 @@ def test_tiled_pipe_graph_replay_equals_eager():
         torch.cuda.synchronize(dev)
         assert torch.equal(a, b)
     assert graphed.tokens == eager.tokens
+
+
+def test_crop_staging_is_reused_across_renders():
+    """render_tiled keeps its pinned/device crop staging between calls (reserve_staging
+    allocates it ahead): back-to-back renders of different host videos through the same
+    buffers each equal the render of that video cropped on the device."""
+    from flashvsr_sm89_ops_b200 import tiling
+    g = torch.Generator().manual_seed(9)
+    C, F, H, W = 3, 5, 1536, 2688
+    kw = dict(num_frames=F, tile_target=700_000, tile_threshold=700_000, device="cuda")
+    videos = [(torch.rand(C, F, H, W, generator=g) * 2 - 1).to(torch.bfloat16) for _ in range(2)]
+    tiling.release_staging()
+    tiling.reserve_staging(videos[0], tile_target=700_000, tile_threshold=700_000, device="cuda")
+    st = next(iter(tiling._STAGING.values()))
+    outs = [render_tiled(_pipe, v, **kw) for v in videos]
+    torch.cuda.synchronize()
+    assert next(iter(tiling._STAGING.values())) is st
+    for v, out in zip(videos, outs):
+        assert torch.equal(out, render_tiled(_pipe, v.cuda(), **kw))
+    tiling.release_staging()
+    assert not tiling._STAGING
