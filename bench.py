@@ -58,14 +58,21 @@ def parse():
 
 
 # kernels of one block at the step's shape, runnable in isolation (--only)
-ONLY_KERNELS = ("attention", "cross_attention", "gemm_qkv", "gemm_o", "ffn", "ln_mod_fp8",
-                "rms_rope", "gate_add", "causal_mask")
+ONLY_KERNELS = ("attention", "cross_attention", "gemm_qkv", "gemm_o", "gemm_up_gelu", "gemm_down",
+                "ffn", "quant_hidden", "quant_token", "ln_mod_fp8", "gate_add_ln_mod_fp8",
+                "gate_add_norm3_fp8", "rms_rope", "gate_add", "pool", "window", "causal_mask",
+                "mask_csr")
+L2_BYTES = 126 << 20
 
 
 def run_only(args, local_rank):
-    """Run one kernel class K times at the workload's shapes; report time and roofline."""
-    from flashvsr_sm89_ops_b200 import fused_gate_add, fused_ln_modulate, lcsa, quantize_fp8
+    """Run one kernel class K times at the workload's shapes; report time and roofline.
+
+    Memory-bound kernels cycle through enough independent input sets to cover three times
+    the L2, so every call reads its operands from HBM as in the step."""
+    from flashvsr_sm89_ops_b200 import _lib, fused_gate_add, fused_ln_modulate, lcsa, quantize_fp8
     from flashvsr_sm89_ops_b200.fp8_linear import fp8_mm
+    from flashvsr_sm89_ops_b200.fused_adaln import gate_add_layer_norm, gate_add_ln_modulate
     from flashvsr_sm89_ops_b200.fused_rms_rope import rms_rope_rows
     from flashvsr_sm89_ops_b200.fp8_ffn import ffn_fp8
     dev = torch.device("cuda", local_rank)
@@ -76,16 +83,28 @@ def run_only(args, local_rank):
     per_row = (lat_h // 8) * (lat_w // 8)
     peaks, kind = load_peaks()
     rnd = lambda *s: torch.randn(*s, generator=g, device=dev).to(torch.bfloat16)  # noqa: E731
+    st = _lib.stream_of(rnd(1))
 
     def wq(n, k):
         from flashvsr_sm89_ops_b200.fp8_linear import quantize_weight
         return quantize_weight(0.02 * torch.randn(n, k, generator=g, device=dev).to(torch.bfloat16), "token")
 
-    x = rnd(L, D)
-    x8, sx = quantize_fp8(x, "token")
+    def rotating(make, set_bytes):
+        """Callable cycling over independent input sets (3x L2 in total) built by make()."""
+        n = max(1, min(16, -(-3 * L2_BYTES // max(set_bytes, 1))))
+        fns = [make() for _ in range(n)]
+        i = [0]
+
+        def fn():
+            fns[i[0] % n]()
+            i[0] += 1
+        return fn
+
+    x8, sx = quantize_fp8(rnd(L, D), "token")
     work, bound = None, "hbm"
+    k_rows = (KV_LEN + 1) * per_row * 128
     if args.only == "attention":
-        q, k, v = rnd(L, D), rnd((KV_LEN + 1) * per_row * 128, D), rnd((KV_LEN + 1) * per_row * 128, D)
+        q, k, v = rnd(L, D), rnd(k_rows, D), rnd(k_rows, D)
         keep = lcsa.causal_topk_mask(q, k, HEADS, per_row, RATIO)
         sel, cnt, _ = lcsa.build_csr(keep)
         out = torch.empty_like(q)
@@ -96,43 +115,113 @@ def run_only(args, local_rank):
         out = torch.empty_like(q)
         fn = lambda: lcsa.dense_attention(q, k, v, HEADS, out=out)  # noqa: E731
         work, bound = L * CTX * 4 * D, "tensor"
-    elif args.only in ("gemm_qkv", "gemm_o"):
-        n = 3 * D if args.only == "gemm_qkv" else D
-        w8, sw = wq(n, D)
+    elif args.only in ("gemm_qkv", "gemm_o", "gemm_down"):
+        n, kk = {"gemm_qkv": (3 * D, D), "gemm_o": (D, D), "gemm_down": (D, FFN)}[args.only]
+        a8, sa = (x8, sx) if kk == D else quantize_fp8(rnd(L, kk), "token")
+        w8, sw = wq(n, kk)
         out = torch.empty(L, n, dtype=torch.bfloat16, device=dev)
-        fn = lambda: fp8_mm(x8, sx, w8, sw, None, out=out)  # noqa: E731
-        work, bound = 2 * L * n * D, "tensor"
+        fn = lambda: fp8_mm(a8, sa, w8, sw, None, out=out)  # noqa: E731
+        work, bound = 2 * L * n * kk, "tensor"
+    elif args.only == "gemm_up_gelu":
+        w8, sw = wq(FFN, D)
+        b = rnd(FFN)
+        h = torch.empty(L, FFN, dtype=torch.bfloat16, device=dev)
+        amax = torch.zeros(L, device=dev)
+        fn = lambda: fp8_mm(x8, sx, w8, sw, b, out=h, epilogue=_lib.FVB_EPI_GELU_AMAX,  # noqa: E731
+                            amax_out=amax)
+        work, bound = 2 * L * FFN * D, "tensor"
     elif args.only == "ffn":
         from flashvsr_sm89_ops_b200.fp8_linear import FP8Linear
         l0 = torch.nn.Linear(D, FFN).to(torch.bfloat16).to(dev)
         l2 = torch.nn.Linear(FFN, D).to(torch.bfloat16).to(dev)
         f0, f2 = FP8Linear(l0, "token"), FP8Linear(l2, "token")
+        res, gate = rnd(1, L, D), rnd(1, 1, D)
         out = torch.empty(L, D, dtype=torch.bfloat16, device=dev)
         ws = torch.empty(2 * L * FFN * 3, dtype=torch.uint8, device=dev)
-        fn = lambda: ffn_fp8(x8, sx, f0, f2, out=out, workspace=ws)  # noqa: E731
+        # the block's call: FFN with the closing gated residual add in its epilogue
+        fn = lambda: ffn_fp8(x8, sx, f0, f2, out=out, workspace=ws, residual=res, gate=gate)  # noqa: E731
         work, bound = 4 * L * D * FFN, "tensor"
+    elif args.only == "quant_hidden":
+        def make():
+            h = rnd(L, FFN)
+            amax = h.float().abs().amax(dim=1).contiguous()
+            q = torch.empty(L, FFN, dtype=torch.float8_e4m3fn, device=dev)
+            sc = torch.empty(L, device=dev)
+            return lambda: _lib.call("fvb_quant_fp8_with_amax", _lib.ptr(h), L, FFN, _lib.ptr(amax),
+                                     _lib.FVB_SCALE_ROW, _lib.ptr(q), _lib.ptr(sc), st)
+        work = L * FFN * 3 + L * 8
+        fn = rotating(make, work)
+    elif args.only == "quant_token":
+        def make():
+            xx = rnd(L, D)
+            return lambda: quantize_fp8(xx, "token")
+        work = L * D * 3 + L * 4
+        fn = rotating(make, work)
     elif args.only == "ln_mod_fp8":
         sc, sh = rnd(1, 1, D), rnd(1, 1, D)
-        x3 = x.view(1, L, D)
-        fn = lambda: fused_ln_modulate(x3, sc, sh, emit_fp8=True)  # noqa: E731
-        work = L * D * (2 + 2 + 1) + L * 4
+
+        def make():
+            x3 = rnd(1, L, D)
+            return lambda: fused_ln_modulate(x3, sc, sh, emit_fp8=True, want_out=False)
+        work = L * D * (2 + 1) + L * 4
+        fn = rotating(make, work)
+    elif args.only == "gate_add_ln_mod_fp8":
+        sc, sh = rnd(1, 1, D), rnd(1, 1, D)
+
+        def make():
+            x3, r3 = rnd(1, L, D), rnd(1, L, D)
+            return lambda: gate_add_ln_modulate(x3, None, r3, sc, sh, emit_fp8=True, want_out=False)
+        work = L * D * 7 + L * 4
+        fn = rotating(make, work)
+    elif args.only == "gate_add_norm3_fp8":
+        gt, w, b = rnd(1, 1, D), rnd(D), rnd(D)
+
+        def make():
+            x3, r3 = rnd(1, L, D), rnd(1, L, D)
+            return lambda: gate_add_layer_norm(x3, gt, r3, w, b, emit_fp8=True, want_out=False)
+        work = L * D * 7 + L * 4
+        fn = rotating(make, work)
     elif args.only == "rms_rope":
         cos = torch.rand(L, 64, generator=g, device=dev)
         sin = torch.rand(L, 64, generator=g, device=dev)
         w = rnd(D)
-        out = torch.empty_like(x)
-        fn = lambda: rms_rope_rows(x, w, cos, sin, L, 1e-6, True, 128, out=out)  # noqa: E731
+
+        def make():
+            xx, out = rnd(L, D), torch.empty(L, D, dtype=torch.bfloat16, device=dev)
+            return lambda: rms_rope_rows(xx, w, cos, sin, L, 1e-6, True, 128, out=out)
         work = L * D * 4 + L * 64 * 8
+        fn = rotating(make, work)
     elif args.only == "gate_add":
-        r, gt = rnd(1, L, D), rnd(1, 1, D)
-        x3 = x.view(1, L, D)
-        out = torch.empty_like(x3)
-        fn = lambda: fused_gate_add(x3, gt, r, out=out)  # noqa: E731
+        gt = rnd(1, 1, D)
+
+        def make():
+            x3, r3 = rnd(1, L, D), rnd(1, L, D)
+            out = torch.empty_like(x3)
+            return lambda: fused_gate_add(x3, gt, r3, out=out)
         work = L * D * 6
+        fn = rotating(make, work)
+    elif args.only == "pool":
+        def make():
+            xw = rnd(L // 128, 128, D)
+            out = torch.empty(L // 128, D, dtype=torch.float32, device=dev)
+            return lambda: lcsa.block_mean_pool(xw, out=out)
+        work = L * D * 2 + (L // 128) * D * 4
+        fn = rotating(make, work)
+    elif args.only == "window":
+        def make():
+            xx = rnd(L, D)
+            out = torch.empty(L // 128, 128, D, dtype=torch.bfloat16, device=dev)
+            return lambda: lcsa.window_partition(xx, (2, lat_h, lat_w), out=out)
+        work = L * D * 4
+        fn = rotating(make, work)
     elif args.only == "causal_mask":
-        q, k = rnd(L, D), rnd((KV_LEN + 1) * per_row * 128, D)
+        q, k = rnd(L, D), rnd(k_rows, D)
         fn = lambda: lcsa.causal_topk_mask(q, k, HEADS, per_row, RATIO)  # noqa: E731
         work = (L + k.shape[0]) * D * 2
+    elif args.only == "mask_csr":
+        keep = torch.rand(HEADS, L // 128, k_rows // 128, generator=g, device=dev) < 0.4
+        fn = lambda: lcsa.build_csr(keep)  # noqa: E731
+        work = keep.numel() * (1 + 4) + HEADS * (L // 128) * 4  # mask in, sel + cnt out
     for _ in range(max(args.warmup, 1)):
         fn()
     torch.cuda.synchronize(dev)
@@ -146,7 +235,7 @@ def run_only(args, local_rank):
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / args.steps
-    fp8 = args.only in ("gemm_qkv", "gemm_o", "ffn")
+    fp8 = args.only in ("gemm_qkv", "gemm_o", "gemm_up_gelu", "gemm_down", "ffn")
     if bound == "tensor" and fp8:
         ach, peak, unit = work / (ms / 1e3) / 1e12, measure_fp8_peak(dev), "TFLOP/s"
         kind = "measured here: cuBLASLt FP8 8192^3 best-of-10"
