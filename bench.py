@@ -59,7 +59,7 @@ def parse():
 
 # kernels of one block at the step's shape, runnable in isolation (--only)
 ONLY_KERNELS = ("attention", "cross_attention", "gemm_qkv", "gemm_o", "gemm_up_gelu", "gemm_down",
-                "ffn", "quant_hidden", "quant_token", "ln_mod_fp8", "gate_add_ln_mod_fp8",
+                "ffn", "gelu_quant_hidden", "quant_hidden", "quant_token", "ln_mod_fp8", "gate_add_ln_mod_fp8",
                 "gate_add_norm3_fp8", "rms_rope", "gate_add", "pool", "window", "causal_mask",
                 "mask_csr")
 L2_BYTES = 126 << 20
@@ -141,6 +141,14 @@ def run_only(args, local_rank):
         # the block's call: FFN with the closing gated residual add in its epilogue
         fn = lambda: ffn_fp8(x8, sx, f0, f2, out=out, workspace=ws, residual=res, gate=gate)  # noqa: E731
         work, bound = 4 * L * D * FFN, "tensor"
+    elif args.only == "gelu_quant_hidden":
+        from flashvsr_sm89_ops_b200.fp8_quant import fused_gelu_quant_fp8
+
+        def make():
+            h = rnd(L, FFN)
+            return lambda: fused_gelu_quant_fp8(h, "token")
+        work = L * FFN * 3 + L * 4
+        fn = rotating(make, work)
     elif args.only == "quant_hidden":
         def make():
             h = rnd(L, FFN)

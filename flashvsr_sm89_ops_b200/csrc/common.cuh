@@ -110,6 +110,39 @@ __device__ __forceinline__ float gelu_tanh_bf16(float x) {
   return bf16r(0.5f * x * (1.0f + tanhf(inner)));
 }
 
+// GELU(tanh) of a bf16 input through a shared-memory table.  The input is 16 bits, so the
+// exact function (gelu_tanh_bf16) is tabulated for |x| in [2^-9, 16) = bf16 bit patterns
+// [0x3B00, 0x4180), 1664 entries per sign (6.5 KB).  Outside the table: 0.5 x for |x| < 2^-9
+// (1 + tanh u rounds to 1 within half a bf16 ulp), x for x >= 16 (tanh u is 1) and x * 0
+// for x <= -16 (tanh u is -1; -0, or NaN for -inf).  Tests push every bf16 value through.
+constexpr uint32_t kGeluLo = 0x3B00u;
+constexpr uint32_t kGeluRange = 0x4180u - kGeluLo;
+constexpr int kGeluTableBytes = (int)(2 * kGeluRange * 2);
+
+__device__ __forceinline__ uint32_t bf16_bits_rn(float x) {
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+// fill the table: thread t of the nthreads sharing the work
+__device__ __forceinline__ void gelu_table_fill(uint16_t* lut, uint32_t t, uint32_t nthreads) {
+  for (uint32_t i = t; i < 2 * kGeluRange; i += nthreads) {
+    const uint32_t neg = i >= kGeluRange;
+    const uint32_t h = (neg << 15) | (kGeluLo + i - neg * kGeluRange);
+    lut[i] = (uint16_t)bf16_bits_rn(gelu_tanh_bf16(__uint_as_float(h << 16)));
+  }
+}
+// bf16 bits of GELU(x) for the bf16 bit pattern h (low 16 bits)
+__device__ __forceinline__ uint32_t gelu_bf16_bits(uint32_t h, const uint16_t* lut) {
+  const uint32_t a = h & 0x7FFFu;
+  const uint32_t k = a - kGeluLo;
+  if (k < kGeluRange) return lut[(h >> 15) * kGeluRange + k];
+  const float x = __uint_as_float(h << 16);
+  return bf16_bits_rn(a < kGeluLo ? 0.5f * x : ((h & 0x8000u) ? x * 0.0f : x));
+}
+// bf16 bits of GELU(bf16(o))
+__device__ __forceinline__ uint32_t gelu_bits(float o, const uint16_t* lut) {
+  return gelu_bf16_bits(bf16_bits_rn(o), lut);
+}
+
 // The scale returned beside the codes, the reference's `amax / FP8_MAX` (fp8_quant.py:54,
 // fp8_ffn.py:72) as torch evaluates it on a CUDA tensor: a division by a host scalar runs as
 // a multiply by the scalar's fp32 reciprocal, fl(amax * fl(1/448)).  (Measured on a B200:
@@ -347,6 +380,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
       "%4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+// contiguous global -> shared copy of `bytes` (a multiple of 16, both addresses 16-byte
+// aligned) whose completion counts on `bar`
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x,

@@ -65,12 +65,10 @@ struct Args {
 
 constexpr int kStageBytes = 32 * 128;  // one epilogue warp's 32 rows x 64 bf16 columns
 
-// GELU table: bf16 bit patterns with |x| in [2^-9, 16) = [0x3B00, 0x4180), both signs
-constexpr uint32_t kGeluLo = 0x3B00u;
-constexpr uint32_t kGeluRange = 0x4180u - kGeluLo;  // 1664 entries per sign
+// the GELU table (gelu_bf16_bits, common.cuh) in shared memory, GELU epilogue only
 template <int EPI>
 struct Lut {
-  static constexpr int kBytes = EPI == FVB_EPI_GELU_AMAX ? (int)(2 * kGeluRange * 2) : 0;
+  static constexpr int kBytes = EPI == FVB_EPI_GELU_AMAX ? kGeluTableBytes : 0;
 };
 
 // W rows one CTA stages per K block: all BN, or its half of the pair's BN
@@ -84,20 +82,6 @@ constexpr size_t smem_bytes() {
   return (size_t)Cfg<EPI, PAIR>::kStages * (BM + b_rows<BN, PAIR>()) * BK +
          (size_t)Cfg<EPI, PAIR>::kEpiWarps * kStageBytes + Lut<EPI>::kBytes +
          1024 /*align slack*/ + 256 /*barriers*/;
-}
-
-__device__ __forceinline__ uint32_t bf16_bits_rn(float x) {
-  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x));
-}
-
-// bf16 bits of GELU(bf16(o)) through the shared-memory table (see the header comment)
-__device__ __forceinline__ uint32_t gelu_bits(float o, const uint16_t* lut) {
-  const uint32_t h = bf16_bits_rn(o);
-  const uint32_t a = h & 0x7FFFu;
-  const uint32_t k = a - kGeluLo;
-  if (k < kGeluRange) return lut[(h >> 15) * kGeluRange + k];
-  const float x = __uint_as_float(h << 16);
-  return bf16_bits_rn(a < kGeluLo ? 0.5f * x : ((h & 0x8000u) ? x * 0.0f : x));
 }
 
 // PAIR: launched as 2-CTA clusters.  The pair owns 256-row x BN tiles: CTA r stages A
@@ -294,11 +278,7 @@ __global__ void __launch_bounds__(Cfg<EPI, PAIR>::kThreads, 1)
     const int half = (warp - 2) >> 2;     // 0..G-1: this warp's first chunk
     if (EPI == FVB_EPI_GELU_AMAX) {
       // tabulate GELU while the first tile's main loop runs; epilogue warps only
-      for (uint32_t i = threadIdx.x - 64; i < 2 * kGeluRange; i += EPI_WARPS * 32) {
-        const uint32_t neg = i >= kGeluRange;
-        const uint32_t h = (neg << 15) | (kGeluLo + i - neg * kGeluRange);
-        lut[i] = (uint16_t)bf16_bits_rn(gelu_tanh_bf16(__uint_as_float(h << 16)));
-      }
+      gelu_table_fill(lut, threadIdx.x - 64, EPI_WARPS * 32);
       asm volatile("bar.sync 1, %0;" ::"r"(EPI_WARPS * 32) : "memory");
     }
     uint8_t* stg = sOut + (size_t)(warp - 2) * kStageBytes;  // this warp's staging, 32 x 128 B

@@ -146,34 +146,59 @@ __global__ void __launch_bounds__(256, kRowBlocksPerSM) quant_row_kernel(
   row_pipeline<NV>(M, load, body);
 }
 
-// K > 2048: the row is read twice (amax, then quantise), the second pass from L1/L2
+// K > 2048: the row is read twice (amax, then quantise), the second pass from L1/L2.
+// One warp per row, rows strided over a persistent grid.  GELU (GELU(tanh) -> e4m3 of
+// fp8_ffn.py:57-72) goes through the block's shared table of the exact function of the
+// 16-bit input (gelu_bf16_bits), built once per block.
+template <bool GELU>
+__device__ __forceinline__ void load8_lut(const uint4* src, int64_t v, const uint16_t* lut,
+                                          float* f) {
+  uint4 u = __ldg(src + v);
+  if (GELU) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(gelu_bf16_bits(w[i] & 0xFFFFu, lut) << 16);
+      f[2 * i + 1] = __uint_as_float(gelu_bf16_bits(w[i] >> 16, lut) << 16);
+    }
+  } else {
+    bf16x8_to_f32(u, f);
+  }
+}
+
 template <bool GELU>
 __global__ void __launch_bounds__(256) quant_row_long_kernel(const __nv_bfloat16* __restrict__ x,
                                                              int64_t M, int64_t K,
                                                              uint8_t* __restrict__ q,
                                                              float* __restrict__ scale_out) {
+  __shared__ uint16_t lut[GELU ? 2 * kGeluRange : 1];
+  if (GELU) {
+    gelu_table_fill(lut, threadIdx.x, blockDim.x);
+    __syncthreads();
+  }
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= M) return;
-  const uint4* xv = reinterpret_cast<const uint4*>(x + row * K);
-  uint2* qv = reinterpret_cast<uint2*>(q + row * K);
   const int64_t nvec = K >> 3;
-  float m = 0.f;
-  for (int64_t v = lane; v < nvec; v += 32) {
-    float f[8];
-    load8<GELU>(xv, v, f);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
+       row += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x + row * K);
+    uint2* qv = reinterpret_cast<uint2*>(q + row * K);
+    float m = 0.f;
+    for (int64_t v = lane; v < nvec; v += 32) {
+      float f[8];
+      load8_lut<GELU>(xv, v, lut, f);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+    }
+    m = warp_max(m);
+    const float s = quant_scale_from_amax(m);
+    const float rs = __frcp_rn(s);
+    for (int64_t v = lane; v < nvec; v += 32) {
+      float f[8];
+      load8_lut<GELU>(xv, v, lut, f);
+      qv[v] = quant8(f, s, rs);
+    }
+    if (lane == 0) scale_out[row] = returned_scale(m);
   }
-  m = warp_max(m);
-  const float s = quant_scale_from_amax(m);
-  const float rs = __frcp_rn(s);
-  for (int64_t v = lane; v < nvec; v += 32) {
-    float f[8];
-    load8<GELU>(xv, v, f);
-    qv[v] = quant8(f, s, rs);
-  }
-  if (lane == 0) scale_out[row] = returned_scale(m);
 }
 
 // Quantisation with a precomputed amax (the second half of fused_gelu_quant_fp8,
@@ -264,8 +289,9 @@ static int quant_impl(const void* x, int64_t M, int64_t K, void* q, float* scale
       else if (K <= 1536) launch(std::integral_constant<int, 6>{});
       else launch(std::integral_constant<int, 8>{});
     } else {
-      quant_row_long_kernel<GELU><<<(unsigned)need, 256, 0, st>>>((const __nv_bfloat16*)x, M, K,
-                                                                   (uint8_t*)q, scale_out);
+      const int64_t cap = (int64_t)sm_count() * 8;
+      quant_row_long_kernel<GELU><<<(unsigned)(need < cap ? need : cap), 256, 0, st>>>(
+          (const __nv_bfloat16*)x, M, K, (uint8_t*)q, scale_out);
     }
     return check_launch(name);
   }

@@ -178,6 +178,30 @@ def test_gelu_quant_matches_gpu_eager_bitexact(mode):
     assert d.max().item() <= 1 and (d > 0).float().mean().item() < 1e-3
 
 
+@pytest.mark.parametrize("rows", ["every_bf16", "step"])
+def test_gelu_quant_long_rows_bitexact(rows):
+    """Per-token GELU -> FP8 on rows longer than 2048 (the FFN hidden, 8960 wide) runs one
+    warp per row over a shared-memory copy of the row with GELU from a table.  Codes and
+    scales must equal quantize_fp8(F.gelu(h)) on the GPU bit for bit: for every bf16 input
+    value (NaN patterns zeroed; rows holding +-inf included) and at the step's 8448 rows,
+    where each warp takes several rows in turn."""
+    from flashvsr_sm89_ops_b200 import quantize_fp8
+    from flashvsr_sm89_ops_b200.fp8_quant import fused_gelu_quant_fp8
+    K = 8960
+    if rows == "every_bf16":
+        x = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+        x = torch.where(torch.isnan(x), torch.zeros_like(x), x)
+        x = torch.cat([x, torch.zeros(8 * K - x.numel(), dtype=torch.bfloat16)]).view(8, K)
+        h = x[torch.randperm(8, generator=gen(8))].contiguous().to(DEV)
+    else:
+        h = (torch.randn(8448, K, generator=gen(9)) * 2).to(torch.bfloat16).to(DEV)
+    q, s = fused_gelu_quant_fp8(h, "token")
+    qe, se = quantize_fp8(F.gelu(h, approximate="tanh"), "token")
+    assert torch.equal(s, se)
+    neq = (q.view(torch.uint8) != qe.view(torch.uint8)).sum().item()
+    assert neq == 0, f"{neq} codes differ from quantize_fp8(F.gelu(h))"
+
+
 # ----------------------------------------------------------------------------- AdaLN
 def test_gate_add_bitwise():
     from flashvsr_sm89_ops_b200 import fused_gate_add
