@@ -15,6 +15,8 @@ function of the canvas, so it must agree exactly).  The B200 changes are in
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 MULT = 128                # pipeline output grid (px)
@@ -233,6 +235,12 @@ class _TileLoader:
         self.st = _staging_for(device, lq.dtype, _crop_numel(lq, tiles, self.order))
         self.copy_stream = torch.cuda.Stream(device)
         self.pool = ThreadPoolExecutor(1)
+        # a crop is copied by several host threads, split by frames (torch's copy releases
+        # the GIL); the host's cores are shared by the ranks of this machine
+        nproc = os.cpu_count() or 1
+        local = max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
+        self.n_copy = max(1, min(8, nproc // local, lq.shape[1]))
+        self.copiers = ThreadPoolExecutor(self.n_copy) if self.n_copy > 1 else None
         self.pending = self.pool.submit(self._pack, 0) if self.order else None
 
     def _shape(self, k):
@@ -246,7 +254,17 @@ class _TileLoader:
             self.st.up_done[b].synchronize()  # stage b still feeds an upload in flight
         shp = self._shape(k)
         n = shp[0] * shp[1] * shp[2] * shp[3]
-        self.st.stage[b][:n].view(shp).copy_(self.lq[:, :, y:y + h, x:x + w])
+        dst = self.st.stage[b][:n].view(shp)
+        src = self.lq[:, :, y:y + h, x:x + w]
+        if self.copiers is None:
+            dst.copy_(src)
+            return k
+        F = shp[1]
+        cuts = [F * i // self.n_copy for i in range(self.n_copy + 1)]
+        jobs = [self.copiers.submit(dst[:, f0:f1].copy_, src[:, f0:f1])
+                for f0, f1 in zip(cuts[:-1], cuts[1:]) if f1 > f0]
+        for j in jobs:
+            j.result()
         return k
 
     def get(self, k):
@@ -283,6 +301,8 @@ class _TileLoader:
             if self.pending is not None:
                 self.pending.result()
             self.pool.shutdown()
+            if self.copiers is not None:
+                self.copiers.shutdown()
 
 
 def render_tiled(pipe, lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
