@@ -58,10 +58,11 @@ def parse():
 
 
 # kernels of one block at the step's shape, runnable in isolation (--only)
-ONLY_KERNELS = ("attention", "cross_attention", "gemm_qkv", "gemm_o", "gemm_up_gelu", "gemm_down",
+ONLY_KERNELS = ("attention", "cross_attention", "gemm_qkv", "gemm_o", "gemm_up", "gemm_up_gelu",
+                "gemm_down",
                 "ffn", "gelu_quant_hidden", "quant_hidden", "quant_token", "ln_mod_fp8", "gate_add_ln_mod_fp8",
                 "gate_add_norm3_fp8", "rms_rope", "gate_add", "pool", "window", "causal_mask",
-                "mask_csr")
+                "mask_csr", "cublaslt_qkv", "cublaslt_o", "cublaslt_up", "cublaslt_down")
 L2_BYTES = 126 << 20
 
 
@@ -115,12 +116,26 @@ def run_only(args, local_rank):
         out = torch.empty_like(q)
         fn = lambda: lcsa.dense_attention(q, k, v, HEADS, out=out)  # noqa: E731
         work, bound = L * CTX * 4 * D, "tensor"
-    elif args.only in ("gemm_qkv", "gemm_o", "gemm_down"):
-        n, kk = {"gemm_qkv": (3 * D, D), "gemm_o": (D, D), "gemm_down": (D, FFN)}[args.only]
+    elif args.only in ("gemm_qkv", "gemm_o", "gemm_up", "gemm_down"):
+        n, kk = {"gemm_qkv": (3 * D, D), "gemm_o": (D, D), "gemm_up": (FFN, D),
+                 "gemm_down": (D, FFN)}[args.only]
         a8, sa = (x8, sx) if kk == D else quantize_fp8(rnd(L, kk), "token")
         w8, sw = wq(n, kk)
+        b = rnd(n)
         out = torch.empty(L, n, dtype=torch.bfloat16, device=dev)
-        fn = lambda: fp8_mm(a8, sa, w8, sw, None, out=out)  # noqa: E731
+        fn = lambda: fp8_mm(a8, sa, w8, sw, b, out=out)  # noqa: E731
+        work, bound = 2 * L * n * kk, "tensor"
+    elif args.only.startswith("cublaslt_"):
+        # the reference's own GEMM path on this box: torch._scaled_mm (cuBLASLt) with the
+        # per-tensor scales of its FP8Linear, bias in the call, bf16 out, same shapes
+        n, kk = {"cublaslt_qkv": (3 * D, D), "cublaslt_o": (D, D), "cublaslt_up": (FFN, D),
+                 "cublaslt_down": (D, FFN)}[args.only]
+        a8 = torch.randn(L, kk, generator=g, device=dev).to(torch.float8_e4m3fn)
+        w8 = (torch.randn(n, kk, generator=g, device=dev) * 0.02).to(torch.float8_e4m3fn)
+        one = torch.ones((), device=dev)
+        b = rnd(n)
+        fn = lambda: torch._scaled_mm(a8, w8.t(), scale_a=one, scale_b=one, bias=b,  # noqa: E731
+                                      out_dtype=torch.bfloat16)
         work, bound = 2 * L * n * kk, "tensor"
     elif args.only == "gemm_up_gelu":
         w8, sw = wq(FFN, D)
@@ -243,7 +258,8 @@ def run_only(args, local_rank):
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / args.steps
-    fp8 = args.only in ("gemm_qkv", "gemm_o", "gemm_up_gelu", "gemm_down", "ffn")
+    fp8 = args.only in ("gemm_qkv", "gemm_o", "gemm_up", "gemm_up_gelu", "gemm_down", "ffn") or \
+        args.only.startswith("cublaslt_")
     if bound == "tensor" and fp8:
         ach, peak, unit = work / (ms / 1e3) / 1e12, measure_fp8_peak(dev), "TFLOP/s"
         kind = "measured here: cuBLASLt FP8 8192^3 best-of-10"

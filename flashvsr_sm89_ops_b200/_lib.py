@@ -52,6 +52,8 @@ _SIGS = {
                                     _i64, _vp, _vp, _vp, _vp, _vp]),
     "fvb_rms_rope": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _int, _vp, _vp, _vp]),
     "fvb_ln_modulate": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp, _vp, _vp]),
+    "fvb_ln_modulate_adaln": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp, _vp, _vp,
+                                     _vp]),
     "fvb_layer_norm": (_int, [_vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp, _vp]),
     "fvb_gate_add_ln_modulate": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp,
                                          _vp, _vp, _vp]),

@@ -109,15 +109,36 @@ __device__ __forceinline__ void row_stats(const uint4* xr, int lane, int nvec, i
 // GATE: the row is first the gated residual sum x + g * r of gate_add_kernel (stored to
 // x_out), so the add and the norm that follows it read the residual stream once.  out may
 // be nullptr when only the FP8 codes are consumed.
-template <bool EMIT_FP8, int NV, bool GATE, bool FULL>
+// MOD: the block's AdaLN modulation sum is formed here instead of by a separate add:
+// `scale` is the block's modulation [6, D] and `shift` the timestep modulation t_mod
+// [B, 6, D]; chunk c of item b is bf16(modulation[c] + t_mod[b, c]) (one rounding of the exact
+// sum, as torch's bf16 add), scale = chunk 1, shift = chunk 0, and block 0 also stores all
+// six chunks of every item to mod_out [B, 6, D] for the block's later consumers.
+template <bool EMIT_FP8, int NV, bool GATE, bool FULL, bool MOD = false>
 __global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ gate,
     const __nv_bfloat16* __restrict__ r, __nv_bfloat16* __restrict__ x_out,
     const __nv_bfloat16* __restrict__ scale, const __nv_bfloat16* __restrict__ shift,
     int64_t rows, int64_t L, int D, float eps, __nv_bfloat16* __restrict__ out,
-    uint8_t* __restrict__ q8, float* __restrict__ q_scale) {
+    uint8_t* __restrict__ q8, float* __restrict__ q_scale, __nv_bfloat16* __restrict__ mod_out) {
   const int lane = threadIdx.x & 31;
   const int nvec = D >> 3;
+  if (MOD && blockIdx.x == 0) {
+    const int64_t nb = rows / L, per = 6 * (int64_t)nvec;
+    const uint4* mb = reinterpret_cast<const uint4*>(scale);
+    const uint4* mt = reinterpret_cast<const uint4*>(shift);
+    uint4* mo = reinterpret_cast<uint4*>(mod_out);
+    for (int64_t i = threadIdx.x; i < nb * per; i += blockDim.x) {
+      const uint4 u = __ldg(mb + i % per), t = __ldg(mt + i);
+      uint4 o;
+      const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+      const __nv_bfloat162* t2 = reinterpret_cast<const __nv_bfloat162*>(&t);
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) o2[p] = __hadd2_rn(u2[p], t2[p]);
+      mo[i] = o;
+    }
+  }
   auto load = [&](int64_t row, uint4* xr) {
     const uint4* xv = reinterpret_cast<const uint4*>(x + row * D);
 #pragma unroll
@@ -132,9 +153,12 @@ __global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_k
   };
   auto body = [&](int64_t row, uint4* xr) {
     const int64_t b = row / L;
-    // scale / shift rows are shared by all rows of a batch item: L1 hits after the first
-    const uint4* sv = reinterpret_cast<const uint4*>(scale + b * D);
-    const uint4* hv = reinterpret_cast<const uint4*>(shift + b * D);
+    // scale / shift rows are shared by all rows of a batch item: L1 hits after the first.
+    // MOD: chunk 1 (scale) and chunk 0 (shift) of the modulation and of t_mod[b]
+    const uint4* sv = reinterpret_cast<const uint4*>(MOD ? scale + D : scale + b * D);
+    const uint4* hv = reinterpret_cast<const uint4*>(MOD ? scale : shift + b * D);
+    const uint4* tsv = reinterpret_cast<const uint4*>(shift + b * 6 * (int64_t)D + D);
+    const uint4* thv = reinterpret_cast<const uint4*>(shift + b * 6 * (int64_t)D);
     float mean, rden;
     row_stats<NV, FULL>(xr, lane, nvec, D, eps, mean, rden);
     const uint64_t nm = f2_pack(-mean, -mean), rd = f2_pack(rden, rden);
@@ -147,7 +171,19 @@ __global__ void __launch_bounds__(256, GATE ? 2 : kRowBlocksPerSM) ln_modulate_k
       if (FULL || v < nvec) {
         float f[8];
         bf16x8_to_f32(xr[j], f);
-        const uint4 su = __ldg(sv + v), hu = __ldg(hv + v);
+        uint4 su = __ldg(sv + v), hu = __ldg(hv + v);
+        if (MOD) {
+          const uint4 ts = __ldg(tsv + v), th = __ldg(thv + v);
+          __nv_bfloat162* s2m = reinterpret_cast<__nv_bfloat162*>(&su);
+          __nv_bfloat162* h2m = reinterpret_cast<__nv_bfloat162*>(&hu);
+          const __nv_bfloat162* ts2 = reinterpret_cast<const __nv_bfloat162*>(&ts);
+          const __nv_bfloat162* th2 = reinterpret_cast<const __nv_bfloat162*>(&th);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            s2m[p] = __hadd2_rn(s2m[p], ts2[p]);
+            h2m[p] = __hadd2_rn(h2m[p], th2[p]);
+          }
+        }
         const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&su);
         const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&hu);
         uint4 yo;
@@ -413,7 +449,7 @@ static void dispatch_nv(int64_t D, F&& f) {
 static int ln_modulate_impl(const void* x, const void* gate, const void* r, void* x_out,
                             const void* scale, const void* shift, int64_t B, int64_t L, int64_t D,
                             float eps, void* out, void* q8, float* q_scale, fvb_stream_t stream,
-                            const char* name) {
+                            const char* name, void* mod_out = nullptr) {
   const int64_t rows = B * L;
   FVB_REQUIRE(x && scale && shift && (out || q8), "%s: NULL pointer", name);
   FVB_REQUIRE(aligned16(x) && aligned16(scale) && aligned16(shift) && (!out || aligned16(out)),
@@ -422,11 +458,22 @@ static int ln_modulate_impl(const void* x, const void* gate, const void* r, void
   auto launch = [&](auto emit, auto nv, auto gated) {
     constexpr int NV = decltype(nv)::value;
     auto go = [&](auto full) {
-      ln_modulate_kernel<decltype(emit)::value, NV, decltype(gated)::value, decltype(full)::value>
-          <<<row_grid(rows, gated ? 2 : kRowBlocksPerSM), 256, 0, (cudaStream_t)stream>>>(
-              (const __nv_bfloat16*)x, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)r,
-              (__nv_bfloat16*)x_out, (const __nv_bfloat16*)scale, (const __nv_bfloat16*)shift,
-              rows, L, (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale);
+      constexpr bool E = decltype(emit)::value, G = decltype(gated)::value,
+                     FL = decltype(full)::value;
+      const unsigned grid = row_grid(rows, G ? 2 : kRowBlocksPerSM);
+      if constexpr (!G && E) {
+        if (mod_out != nullptr) {
+          ln_modulate_kernel<E, NV, false, FL, true><<<grid, 256, 0, (cudaStream_t)stream>>>(
+              (const __nv_bfloat16*)x, nullptr, nullptr, nullptr, (const __nv_bfloat16*)scale,
+              (const __nv_bfloat16*)shift, rows, L, (int)D, eps, (__nv_bfloat16*)out,
+              (uint8_t*)q8, q_scale, (__nv_bfloat16*)mod_out);
+          return;
+        }
+      }
+      ln_modulate_kernel<E, NV, G, FL><<<grid, 256, 0, (cudaStream_t)stream>>>(
+            (const __nv_bfloat16*)x, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)r,
+            (__nv_bfloat16*)x_out, (const __nv_bfloat16*)scale, (const __nv_bfloat16*)shift,
+            rows, L, (int)D, eps, (__nv_bfloat16*)out, (uint8_t*)q8, q_scale, nullptr);
     };
     // (the plain bf16-output form spills in its FULL build at this register budget)
     if (D == NV * 256 && (decltype(emit)::value || decltype(gated)::value)) go(std::true_type{});
@@ -491,6 +538,21 @@ int fvb_ln_modulate(const void* x, const void* scale, const void* shift, int64_t
   if (B * L == 0) return FVB_OK;
   return ln_modulate_impl(x, nullptr, nullptr, nullptr, scale, shift, B, L, D, eps, out, q8,
                           q_scale, stream, "fvb_ln_modulate");
+}
+
+int fvb_ln_modulate_adaln(const void* x, const void* modulation, const void* t_mod, int64_t B,
+                          int64_t L, int64_t D, float eps, void* out, void* q8, float* q_scale,
+                          void* mod_out, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(B >= 0 && L >= 0 && D > 0, "fvb_ln_modulate_adaln: bad shape");
+  FVB_REQUIRE(D % 8 == 0 && D <= 2048, "fvb_ln_modulate_adaln: D must be a multiple of 8, <= 2048");
+  FVB_REQUIRE(q8 != nullptr && q_scale != nullptr,
+              "fvb_ln_modulate_adaln: q8 and q_scale are required (the FP8-emitting norm)");
+  if (B * L == 0) return FVB_OK;
+  FVB_REQUIRE(mod_out != nullptr && aligned16(mod_out), "fvb_ln_modulate_adaln: mod_out NULL or "
+              "not 16-byte aligned");
+  return ln_modulate_impl(x, nullptr, nullptr, nullptr, modulation, t_mod, B, L, D, eps, out, q8,
+                          q_scale, stream, "fvb_ln_modulate_adaln", mod_out);
 }
 
 int fvb_gate_add_ln_modulate(const void* x, const void* gate, const void* r, void* x_out,

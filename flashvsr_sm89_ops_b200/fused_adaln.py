@@ -50,6 +50,34 @@ def fused_ln_modulate(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
     return out
 
 
+def fused_ln_modulate_adaln(x: torch.Tensor, modulation: torch.Tensor, t_mod: torch.Tensor,
+                            eps: float = 1e-6, emit_fp8: bool = True, want_out: bool = True):
+    """The DiT block's first norm with its modulation sum in the same launch.
+
+    Equals ``mod = modulation + t_mod`` (bf16, [B, 6, D]) followed by
+    ``fused_ln_modulate(x, mod[:, 1:2], mod[:, 0:1], eps, emit_fp8=True)`` bit for bit
+    (integrate.py:154-158).  modulation [1, 6, D], t_mod [B, 6, D], both bf16.
+    Returns (out, q8, scale, mod); out is None when want_out=False.
+    """
+    if not emit_fp8:
+        raise ValueError("fused_ln_modulate_adaln: only the FP8-emitting form exists")
+    _check(x, "fused_ln_modulate_adaln")
+    B, L, D = x.shape
+    if modulation.dtype != torch.bfloat16 or t_mod.dtype != torch.bfloat16:
+        raise ValueError("fused_ln_modulate_adaln: modulation/t_mod must be bf16")
+    if modulation.numel() != 6 * D or t_mod.shape != (B, 6, D):
+        raise ValueError("fused_ln_modulate_adaln: modulation [1, 6, D], t_mod [B, 6, D]")
+    assert x.is_contiguous() and modulation.is_contiguous() and t_mod.is_contiguous()
+    out = torch.empty_like(x) if want_out else None
+    mod = torch.empty((B, 6, D), dtype=torch.bfloat16, device=x.device)
+    q8 = torch.empty((B * L, D), dtype=torch.float8_e4m3fn, device=x.device)
+    qs = torch.empty((B * L,), dtype=torch.float32, device=x.device)
+    _lib.call("fvb_ln_modulate_adaln", _lib.ptr(x), _lib.ptr(modulation), _lib.ptr(t_mod), B, L,
+              D, float(eps), _lib.ptr(out), _lib.ptr(q8), _lib.ptr(qs), _lib.ptr(mod),
+              _lib.stream_of(x))
+    return out, q8, qs, mod
+
+
 def fused_gate_add(x: torch.Tensor, gate: torch.Tensor | None, residual: torch.Tensor,
                    out: torch.Tensor | None = None):
     """x + gate * residual. x/residual [B, L, D] contiguous bf16; gate [B, 1, D] (None: x + r)."""

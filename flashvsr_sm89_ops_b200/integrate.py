@@ -33,8 +33,8 @@ from .compat_bsa import active_backend, ensure_bsa_available
 from .fp8_ffn import FP8FFN, convert_ffn_fp8, ffn_fp8
 from .fp8_linear import FP8Linear, convert_linears_fp8, fp8_mm
 from .fp8_quant import default_act_mode, quantize_fp8
-from .fused_adaln import (fused_gate_add, fused_ln_modulate, gate_add_layer_norm,
-                          gate_add_ln_modulate, layer_norm)
+from .fused_adaln import (fused_gate_add, fused_ln_modulate, fused_ln_modulate_adaln,
+                          gate_add_layer_norm, gate_add_ln_modulate, layer_norm)
 from .fused_rms_rope import freqs_cos_sin, fused_rms_rope, rms_rope_rows
 
 
@@ -349,20 +349,35 @@ def _make_dit_block_forward(dit):
     def forward(self, x, context, t_mod, freqs, f, h, w, local_num=None, topk=None,
                 train_img=False, block_id=None, kv_len=None, is_full_block=False,
                 is_stream=False, pre_cache_k=None, pre_cache_v=None, local_range=9):
-        shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (
-            self.modulation.to(dtype=t_mod.dtype, device=t_mod.device) + t_mod).chunk(6, dim=1)
         fa = getattr(dit, "FUSED_ADALN", None)
         fast = fa is not None and fa[0] is fused_ln_modulate and x.shape[0] == 1 and x.is_cuda
         token = fast and default_act_mode() == "token"
+        fp8_norm1 = token and _qkv_pack(self.self_attn) is not None \
+            and self.self_attn.q.mode == "token"
+        mod_p = self.modulation
+        # norm1 forms the modulation sum in its own launch when both operands are the bf16
+        # device tensors the kernel takes
+        fused_mod = fp8_norm1 and mod_p.dtype == t_mod.dtype == torch.bfloat16 and mod_p.is_cuda \
+            and t_mod.is_cuda and t_mod.dim() == 3 and t_mod.shape[1] == 6 \
+            and mod_p.is_contiguous() and t_mod.is_contiguous()
+        if not fused_mod:
+            shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (
+                mod_p.to(dtype=t_mod.dtype, device=t_mod.device) + t_mod).chunk(6, dim=1)
         if fa is not None:
             ln_mod, gate_add = fa
-            if token and _qkv_pack(self.self_attn) is not None and self.self_attn.q.mode == "token":
+            if fp8_norm1:
                 # the fast self-attention path reads only the FP8 codes: no bf16 output then
                 # (the block input stands in for it as the stash key)
                 skip = _self_fast_path(dit, self.self_attn, x)
-                input_x, x8, s8 = fused_ln_modulate(x, scale_msa, shift_msa,
-                                                    eps=_module_eps(self.norm1), emit_fp8=True,
-                                                    want_out=not skip)
+                eps1 = _module_eps(self.norm1)
+                if fused_mod:
+                    input_x, x8, s8, mod = fused_ln_modulate_adaln(
+                        x, mod_p, t_mod, eps=eps1, emit_fp8=True, want_out=not skip)
+                    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = \
+                        mod.chunk(6, dim=1)
+                else:
+                    input_x, x8, s8 = fused_ln_modulate(x, scale_msa, shift_msa, eps=eps1,
+                                                        emit_fp8=True, want_out=not skip)
                 input_x = x if input_x is None else input_x
                 self.self_attn._fvb_x8 = (input_x, x8.view(-1, x.shape[-1]), s8)
             else:

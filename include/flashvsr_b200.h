@@ -162,6 +162,18 @@ FVB_API int fvb_ln_modulate(const void* x, const void* scale, const void* shift,
                     int64_t D, float eps, void* out, void* q8, float* q_scale,
                     fvb_stream_t stream);
 
+/* The DiT block's first norm with its AdaLN modulation sum formed in the same launch
+ * (replaces `(self.modulation + t_mod).chunk(6, dim=1)` followed by fused_ln_modulate
+ * with chunks 1 and 0, integrate.py:154-158):
+ *   mod_out[b, c, :] = bf16(modulation[c, :] + t_mod[b, c, :])   (c = 0..5, one rounding,
+ *                                                                  as torch's bf16 add)
+ *   out = fvb_ln_modulate(x, scale = mod_out[:, 1], shift = mod_out[:, 0]) bit for bit.
+ * modulation [6, D] (the block's [1, 6, D] parameter), t_mod [B, 6, D], mod_out [B, 6, D],
+ * all bf16, contiguous, 16-byte aligned; q8/q_scale are required, out may be NULL. */
+FVB_API int fvb_ln_modulate_adaln(const void* x, const void* modulation, const void* t_mod,
+                                  int64_t B, int64_t L, int64_t D, float eps, void* out, void* q8,
+                                  float* q_scale, void* mod_out, fvb_stream_t stream);
+
 /* LayerNorm with affine weight/bias (the block's norm3: torch.nn.LayerNorm on bf16, which the
  * reference leaves to PyTorch, wan_video_dit DiTBlock.norm3):
  *   out = bf16( (x-mean)/sqrt(var+eps) * w + b )   fp32 math, one rounding

@@ -714,3 +714,29 @@ def test_causal_topk_mask_ties_take_lower_index():
         for i in range(per_row):
             n = int(taken[h, i])
             assert kp[h, i, :n].all() and not kp[h, i, n:].any()
+
+
+@pytest.mark.parametrize("B,L,D", [(1, 8448, 1536), (2, 37, 256)])
+@pytest.mark.parametrize("want_out", [True, False])
+def test_ln_modulate_adaln_equals_add_then_ln_modulate(B, L, D, want_out):
+    """norm1 with the block's modulation sum in the same launch equals the eager
+    `modulation + t_mod` followed by fused_ln_modulate on chunks 1 (scale) and 0 (shift), bit
+    for bit: the six summed chunks, the bf16 output and the FP8 codes and scales."""
+    from flashvsr_sm89_ops_b200 import fused_ln_modulate
+    from flashvsr_sm89_ops_b200.fused_adaln import fused_ln_modulate_adaln
+    g = gen(41)
+    x = (torch.randn(B, L, D, generator=g) * 2).to(torch.bfloat16).to(DEV)
+    modulation = (torch.randn(1, 6, D, generator=g) / D ** 0.5).to(torch.bfloat16).to(DEV)
+    t_mod = torch.randn(B, 6, D, generator=g).to(torch.bfloat16).to(DEV)
+    out, q8, qs, mod = fused_ln_modulate_adaln(x, modulation, t_mod, emit_fp8=True,
+                                               want_out=want_out)
+    ref_mod = modulation + t_mod
+    assert torch.equal(mod, ref_mod)
+    shift, scale = ref_mod[:, 0:1].contiguous(), ref_mod[:, 1:2].contiguous()
+    ro, rq, rs = fused_ln_modulate(x, scale, shift, emit_fp8=True)
+    if want_out:
+        assert torch.equal(out, ro)
+    else:
+        assert out is None
+    assert torch.equal(q8.view(torch.uint8), rq.view(torch.uint8))
+    assert torch.equal(qs, rs)
