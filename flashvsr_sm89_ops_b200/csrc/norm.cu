@@ -34,7 +34,10 @@ __device__ __forceinline__ uint2 fp8_codes8(const uint4& y, float qs, float rqs)
 
 // Gated residual add of one row held in registers (the gate_add_kernel arithmetic):
 // x <- bf16(x + bf16(g * r)) (g == nullptr: bf16(x + r)), also stored to xo; raw holds
-// the row's x vectors then its r vectors.
+// the row's x vectors then its r vectors.  Packed bf16 _rn operations: the product of two
+// bf16 values is exact in fp32, and an fp32 sum of two bf16 values rounds to the same bf16
+// as their exact sum, so the eager fp32 chain and one rounding per operation agree bit for
+// bit (as in the FFN-down epilogue's gated residual add).
 template <int NV, bool FULL>
 __device__ __forceinline__ void gate_add_row(const uint4* raw, uint4* xr, int lane, int nvec,
                                              const __nv_bfloat16* g, uint4* xo) {
@@ -42,20 +45,21 @@ __device__ __forceinline__ void gate_add_row(const uint4* raw, uint4* xr, int la
   for (int j = 0; j < NV; ++j) {
     const int v = j * 32 + lane;
     if (FULL || v < nvec) {
-      float xf[8], rf[8];
-      bf16x8_to_f32(raw[j], xf);
-      bf16x8_to_f32(raw[NV + j], rf);
+      uint4 o = raw[j];
+      const uint4 ru = raw[NV + j];
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&ru);
       if (g) {
-        float gf[8];
-        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(g) + v), gf);
+        const uint4 gu = __ldg(reinterpret_cast<const uint4*>(g) + v);
+        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gu);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) xf[i] = xf[i] + bf16r(gf[i] * rf[i]);
+        for (int p = 0; p < 4; ++p) o2[p] = __hadd2_rn(o2[p], __hmul2_rn(g2[p], r2[p]));
       } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) xf[i] = xf[i] + rf[i];
+        for (int p = 0; p < 4; ++p) o2[p] = __hadd2_rn(o2[p], r2[p]);
       }
-      xr[j] = f32_to_bf16x8(xf);
-      xo[v] = xr[j];
+      xr[j] = o;
+      xo[v] = o;
     }
   }
 }
@@ -318,23 +322,36 @@ __global__ void __launch_bounds__(256) gate_add_kernel(const uint4* __restrict__
                                                         const __nv_bfloat16* __restrict__ gate,
                                                         const uint4* __restrict__ r, int64_t nvec,
                                                         int64_t LD, int D, uint4* __restrict__ out) {
+  // gate is [B, 1, D]: vector v of the [B, L, D] stream takes gate vector
+  // (v / (L*D/8)) * (D/8) + v % (D/8); 32-bit index math when the stream allows it
+  const uint32_t nvd = (uint32_t)(D >> 3);
+  const int64_t per_b = LD >> 3;
+  const bool small = nvec <= 0xFFFFFFFFll && per_b <= 0xFFFFFFFFll;
   for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
        v += (int64_t)gridDim.x * blockDim.x) {
-    float xf[8], rf[8];
-    bf16x8_to_f32(__ldg(x + v), xf);
-    bf16x8_to_f32(__ldg(r + v), rf);
+    uint4 o = __ldg(x + v);
+    const uint4 ru = __ldg(r + v);
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+    const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&ru);
     if (gate) {
-      const int64_t idx = v * 8;
-      const int64_t p = (idx / LD) * D + (idx % D);  // gate is [B, 1, D]
-      float gf[8];
-      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(gate + p)), gf);
+      int64_t gv;
+      if (small) {
+        const uint32_t v32 = (uint32_t)v, pb = (uint32_t)per_b;
+        const uint32_t b = v32 / pb;
+        gv = (int64_t)b * nvd + (v32 - b * pb) % nvd;
+      } else {
+        gv = (v / per_b) * nvd + (v % per_b) % nvd;
+      }
+      const uint4 gu = __ldg(reinterpret_cast<const uint4*>(gate) + gv);
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gu);
+      // bf16(x + bf16(g * r)) with one rounding per operation (see gate_add_row)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) xf[i] = xf[i] + bf16r(gf[i] * rf[i]);
+      for (int p = 0; p < 4; ++p) o2[p] = __hadd2_rn(o2[p], __hmul2_rn(g2[p], r2[p]));
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) xf[i] = xf[i] + rf[i];
+      for (int p = 0; p < 4; ++p) o2[p] = __hadd2_rn(o2[p], r2[p]);
     }
-    out[v] = f32_to_bf16x8(xf);
+    out[v] = o;
   }
 }
 
