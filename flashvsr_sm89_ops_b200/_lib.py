@@ -51,6 +51,8 @@ _SIGS = {
     "fvb_fp8_ffn_residual": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _int, _i64, _i64,
                                     _i64, _vp, _vp, _vp, _vp, _vp]),
     "fvb_rms_rope": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _int, _vp, _vp, _vp]),
+    "fvb_qkv_rope_window": (_int, [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32,
+                                   _f32, _vp, _vp, _vp, _vp, _vp]),
     "fvb_ln_modulate": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp, _vp, _vp]),
     "fvb_ln_modulate_adaln": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _f32, _vp, _vp, _vp, _vp,
                                      _vp]),
@@ -67,6 +69,7 @@ _SIGS = {
     "fvb_draft_block_mask": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "fvb_causal_topk_mask": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp]),
     "fvb_block_mean_pool": (_int, [_vp, _i64, _i64, _vp, _vp]),
+    "fvb_block_mean_pool2": (_int, [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _vp]),
     "fvb_causal_topk_pooled": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp]),
 }
 

@@ -81,11 +81,19 @@ __global__ void __launch_bounds__(256) mask_to_csr_kernel(const uint8_t* __restr
 // loads in flight per thread); the 4 partial sums meet in shared memory in a fixed order.
 // The order is part of the keep rules' definition (the oracle restates it): partial g sums
 // tokens g, g+4, ..., g+124 in that order; mean = ((p0 + p1) + (p2 + p3)) / 128.
-__global__ void __launch_bounds__(256) pool_kernel(const __nv_bfloat16* __restrict__ x,
+// TWO: two sources in one launch (grid.x = nblk + nblk2): the first nblk windows come from
+// x into avg, the rest from x2 into avg2.
+template <bool TWO = false>
+__global__ void __launch_bounds__(256) pool_kernel(const __nv_bfloat16* __restrict__ x_in,
                                                     int64_t nblk, int64_t C, int round_bf16,
-                                                    float* __restrict__ avg) {
+                                                    float* __restrict__ avg_in,
+                                                    const __nv_bfloat16* __restrict__ x2 = nullptr,
+                                                    float* __restrict__ avg2 = nullptr) {
   __shared__ float part[4][64][8];
-  const int64_t blk = blockIdx.x;
+  const bool second = TWO && (int64_t)blockIdx.x >= nblk;
+  const int64_t blk = second ? (int64_t)blockIdx.x - nblk : (int64_t)blockIdx.x;
+  const __nv_bfloat16* __restrict__ x = second ? x2 : x_in;
+  float* __restrict__ avg = second ? avg2 : avg_in;
   const int vx = threadIdx.x & 63, ty = threadIdx.x >> 6;
   const int64_t c8 = (int64_t)blockIdx.y * 64 + vx;
   const bool on = c8 * 8 < C;
@@ -463,8 +471,8 @@ int fvb_draft_block_mask(const void* q_w, const void* k_w, int64_t H, int64_t NQ
   float* aq = static_cast<float*>(workspace);
   float* ak = aq + NQ * C;
   float* prob = ak + NK * C;
-  pool_kernel<<<dim3((unsigned)NQ, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)q_w, NQ, C, 1, aq);
-  pool_kernel<<<dim3((unsigned)NK, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 1, ak);
+  pool_kernel<false><<<dim3((unsigned)NQ, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)q_w, NQ, C, 1, aq);
+  pool_kernel<false><<<dim3((unsigned)NK, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 1, ak);
   int rc = check_launch("fvb_draft_block_mask pool");
   if (rc) return rc;
   const size_t smem = (size_t)NK * 4;
@@ -497,8 +505,8 @@ int fvb_causal_topk_mask(const void* q_w, const void* k_w, int64_t H, int64_t NQ
   const int64_t C = H * d;
   float* aq = static_cast<float*>(workspace);
   float* ak = aq + NQ * C;
-  pool_kernel<<<dim3((unsigned)NQ, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)q_w, NQ, C, 0, aq);
-  pool_kernel<<<dim3((unsigned)NK, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 0, ak);
+  pool_kernel<false><<<dim3((unsigned)NQ, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)q_w, NQ, C, 0, aq);
+  pool_kernel<false><<<dim3((unsigned)NK, (unsigned)((C + 511) / 512)), 256, 0, st>>>((const __nv_bfloat16*)k_w, NK, C, 0, ak);
   int rc = check_launch("fvb_causal_topk_mask pool");
   if (rc) return rc;
   return launch_causal_topk(aq, ak, H, NQ, NK, d, per_row, ratio, keep, st);
@@ -509,9 +517,23 @@ int fvb_block_mean_pool(const void* x, int64_t nblk, int64_t C, float* out, fvb_
   FVB_REQUIRE(nblk >= 0 && C > 0 && C % 8 == 0, "fvb_block_mean_pool: shape");
   if (nblk == 0) return FVB_OK;
   FVB_REQUIRE(x && out && aligned16(x), "fvb_block_mean_pool: pointers");
-  pool_kernel<<<dim3((unsigned)nblk, (unsigned)((C + 511) / 512)), 256, 0, (cudaStream_t)stream>>>(
+  pool_kernel<false><<<dim3((unsigned)nblk, (unsigned)((C + 511) / 512)), 256, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)x, nblk, C, 0, out);
   return check_launch("fvb_block_mean_pool");
+}
+
+int fvb_block_mean_pool2(const void* x, int64_t nblk, const void* x2, int64_t nblk2, int64_t C,
+                         float* out, float* out2, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(nblk >= 0 && nblk2 >= 0 && C > 0 && C % 8 == 0, "fvb_block_mean_pool2: shape");
+  FVB_REQUIRE(nblk + nblk2 < (1ll << 31), "fvb_block_mean_pool2: too many windows");
+  if (nblk + nblk2 == 0) return FVB_OK;
+  FVB_REQUIRE((nblk == 0 || (x && out && aligned16(x))) && (nblk2 == 0 || (x2 && out2 && aligned16(x2))),
+              "fvb_block_mean_pool2: pointers");
+  pool_kernel<true><<<dim3((unsigned)(nblk + nblk2), (unsigned)((C + 511) / 512)), 256, 0,
+                      (cudaStream_t)stream>>>((const __nv_bfloat16*)x, nblk, C, 0, out,
+                                              (const __nv_bfloat16*)x2, out2);
+  return check_launch("fvb_block_mean_pool2");
 }
 
 int fvb_causal_topk_pooled(const float* aq, const float* ak, int64_t H, int64_t NQ, int64_t NK,

@@ -367,6 +367,71 @@ __device__ __forceinline__ void unpack_row_f(const uint4* raw, float* f, int lan
 // (mul.rn / add.rn per lane, no contraction), then one bf16 rounding.  rrms =
 // rsqrt(sum(x^2) / D + eps) with the approximate reciprocal square root, as the reference's
 // Triton kernel takes it (tl.rsqrt).
+// One row of RMSNorm (+ RoPE) from the lane's fp32 copy f of the row, written to ov (the
+// output row).  srow: the row's position in the sequence (cos / sin row).
+template <bool ROPE, int NV>
+__device__ __forceinline__ void rms_rope_row(const float* f, int lane, int nvec, float invD,
+                                             float eps, int head_dim, int64_t srow,
+                                             const __nv_bfloat16* __restrict__ w,
+                                             const float* __restrict__ cosv,
+                                             const float* __restrict__ sinv, uint4* ov) {
+  uint64_t q2 = f2_pack(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    if (j * 32 + lane < nvec) {
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const uint64_t t = f2_pack(f[8 * j + i], f[8 * j + i + 1]);
+        q2 = f2_fma(t, t, q2);
+      }
+    }
+  }
+  float qa, qb;
+  f2_unpack(q2, qa, qb);
+  const float rrms = rsqrtf(warp_sum(qa + qb) * invD + eps);
+  const uint64_t rr = f2_pack(rrms, rrms);
+  const int half = head_dim >> 1;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int v = j * 32 + lane;
+    if (v < nvec) {
+      float wf[8];
+      bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), wf);
+      float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f), s4 = c4;
+      if (ROPE) {
+        const int pair0 = ((v * 8) % head_dim) >> 1;  // 4 consecutive pairs
+        c4 = __ldg(reinterpret_cast<const float4*>(cosv + srow * half + pair0));
+        s4 = __ldg(reinterpret_cast<const float4*>(sinv + srow * half + pair0));
+      }
+      const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+      const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
+      uint4 yo;
+      __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&yo);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        float a, b;
+        f2_unpack(f2_mul(f2_pack(f[8 * j + 2 * p], f[8 * j + 2 * p + 1]), rr), a, b);
+        const float2 yb = __bfloat1622float2(__floats2bfloat162_rn(a, b));
+        const uint64_t yw = f2_mul(f2_pack(yb.x, yb.y), f2_pack(wf[2 * p], wf[2 * p + 1]));
+        if (ROPE) {
+          float ye, yo_;
+          f2_unpack(yw, ye, yo_);
+          float e, o;
+          f2_unpack(f2_add(f2_mul(yw, f2_pack(cc[p], cc[p])),
+                           f2_mul(f2_pack(yo_, ye), f2_pack(-ss[p], ss[p]))),
+                    e, o);
+          y2[p] = __floats2bfloat162_rn(e, o);
+        } else {
+          float ye, yo_;
+          f2_unpack(yw, ye, yo_);
+          y2[p] = __floats2bfloat162_rn(ye, yo_);
+        }
+      }
+      ov[v] = yo;
+    }
+  }
+}
+
 template <bool ROPE, int NV>
 __global__ void __launch_bounds__(256, 2) rms_rope_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t x_ld, const __nv_bfloat16* __restrict__ w,
@@ -384,66 +449,56 @@ __global__ void __launch_bounds__(256, 2) rms_rope_kernel(
   };
   auto prep = [&](int64_t, const uint4* raw, float* f) { unpack_row_f<NV>(raw, f, lane, nvec); };
   auto body = [&](int64_t row, float* f) {
-    uint64_t q2 = f2_pack(0.f, 0.f);
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      if (j * 32 + lane < nvec) {
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          const uint64_t t = f2_pack(f[8 * j + i], f[8 * j + i + 1]);
-          q2 = f2_fma(t, t, q2);
-        }
-      }
-    }
-    float qa, qb;
-    f2_unpack(q2, qa, qb);
-    const float rrms = rsqrtf(warp_sum(qa + qb) * invD + eps);
-    const uint64_t rr = f2_pack(rrms, rrms);
-    const int64_t srow = row % L;
-    const int half = head_dim >> 1;
     const int64_t orow = row_map ? (int64_t)__ldg(row_map + row) : row;
-    uint4* ov = reinterpret_cast<uint4*>(out + orow * D);
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int v = j * 32 + lane;
-      if (v < nvec) {
-        float wf[8];
-        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w) + v), wf);
-        float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f), s4 = c4;
-        if (ROPE) {
-          const int pair0 = ((v * 8) % head_dim) >> 1;  // 4 consecutive pairs
-          c4 = __ldg(reinterpret_cast<const float4*>(cosv + srow * half + pair0));
-          s4 = __ldg(reinterpret_cast<const float4*>(sinv + srow * half + pair0));
-        }
-        const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
-        const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
-        uint4 yo;
-        __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&yo);
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          float a, b;
-          f2_unpack(f2_mul(f2_pack(f[8 * j + 2 * p], f[8 * j + 2 * p + 1]), rr), a, b);
-          const float2 yb = __bfloat1622float2(__floats2bfloat162_rn(a, b));
-          const uint64_t yw = f2_mul(f2_pack(yb.x, yb.y), f2_pack(wf[2 * p], wf[2 * p + 1]));
-          if (ROPE) {
-            float ye, yo_;
-            f2_unpack(yw, ye, yo_);
-            float e, o;
-            f2_unpack(f2_add(f2_mul(yw, f2_pack(cc[p], cc[p])),
-                             f2_mul(f2_pack(yo_, ye), f2_pack(-ss[p], ss[p]))),
-                      e, o);
-            y2[p] = __floats2bfloat162_rn(e, o);
-          } else {
-            float ye, yo_;
-            f2_unpack(yw, ye, yo_);
-            y2[p] = __floats2bfloat162_rn(ye, yo_);
-          }
-        }
-        ov[v] = yo;
-      }
-    }
+    rms_rope_row<ROPE, NV>(f, lane, nvec, invD, eps, head_dim, row % L, w, cosv, sinv,
+                           reinterpret_cast<uint4*>(out + orow * D));
   };
   row_pipeline_f<NV, NV>(rows, load, prep, body);
+}
+
+// The self-attention's q, k and v from the fused projection output qkv [rows, 3D] in one
+// launch: rows [0, R) are RMSNorm(w_q) + RoPE of the q third, [R, 2R) the same for k with
+// w_k, [2R, 3R) the v third copied; every output row r goes to row row_map[r] of its output
+// (the window order), exactly as three rms_rope / window_partition launches would write it.
+struct QkvRows {
+  const __nv_bfloat16* x;
+  int64_t x_ld;
+  const __nv_bfloat16* w[2];
+  float eps[2];
+  const int32_t* row_map;
+  __nv_bfloat16* out[3];
+};
+
+template <int NV>
+__global__ void __launch_bounds__(256, 2) qkv_rope_window_kernel(
+    const QkvRows a, const float* __restrict__ cosv, const float* __restrict__ sinv, int64_t R,
+    int64_t L, int D, int head_dim) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = D >> 3;
+  const float invD = 1.0f / (float)D;
+  auto load = [&](int64_t row, uint4* raw) {
+    const int p = (int)(row / R);
+    const uint4* xv = reinterpret_cast<const uint4*>(a.x + (row - p * R) * a.x_ld + p * D);
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+      if (j * 32 + lane < nvec) raw[j] = __ldg(xv + j * 32 + lane);
+  };
+  auto prep = [&](int64_t, const uint4* raw, float* f) { unpack_row_f<NV>(raw, f, lane, nvec); };
+  auto body = [&](int64_t row, float* f) {
+    const int p = (int)(row / R);
+    const int64_t r = row - p * R;
+    const int64_t orow = a.row_map ? (int64_t)__ldg(a.row_map + r) : r;
+    uint4* ov = reinterpret_cast<uint4*>(a.out[p] + orow * D);
+    if (p < 2) {
+      rms_rope_row<true, NV>(f, lane, nvec, invD, a.eps[p], head_dim, r % L, a.w[p], cosv, sinv,
+                             ov);
+    } else {
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+        if (j * 32 + lane < nvec) ov[j * 32 + lane] = f32_to_bf16x8(f + 8 * j);  // exact
+    }
+  };
+  row_pipeline_f<NV, NV>(3 * R, load, prep, body);
 }
 
 static inline unsigned row_grid(int64_t rows, int blocks_per_sm = kRowBlocksPerSM) {
@@ -632,6 +687,43 @@ int fvb_gate_add(const void* x, const void* gate, const void* r, int64_t B, int6
       (const uint4*)x, (const __nv_bfloat16*)gate, (const uint4*)r, nvec, L * D, (int)D,
       (uint4*)out);
   return check_launch("fvb_gate_add");
+}
+
+int fvb_qkv_rope_window(const void* qkv, int64_t x_ld, const void* w_q, const void* w_k,
+                        const float* cos, const float* sin, int64_t rows, int64_t L, int64_t D,
+                        int64_t head_dim, float eps_q, float eps_k, const int32_t* row_map,
+                        void* out_q, void* out_k, void* out_v, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(rows >= 0 && D > 0 && D % 8 == 0 && D <= 2048, "fvb_qkv_rope_window: bad D");
+  if (x_ld == 0) x_ld = 3 * D;
+  FVB_REQUIRE(x_ld >= 3 * D && x_ld % 8 == 0,
+              "fvb_qkv_rope_window: x_ld must be >= 3 D and a multiple of 8");
+  if (rows == 0) return FVB_OK;
+  FVB_REQUIRE(L > 0 && rows % L == 0 && rows < (1ll << 40), "fvb_qkv_rope_window: rows / L");
+  FVB_REQUIRE(qkv && w_q && w_k && out_q && out_k && out_v && cos && sin,
+              "fvb_qkv_rope_window: NULL pointer");
+  FVB_REQUIRE(aligned16(qkv) && aligned16(w_q) && aligned16(w_k) && aligned16(out_q) &&
+                  aligned16(out_k) && aligned16(out_v) && aligned16(cos) && aligned16(sin),
+              "fvb_qkv_rope_window: alignment");
+  FVB_REQUIRE(head_dim > 0 && head_dim % 8 == 0 && D % head_dim == 0,
+              "fvb_qkv_rope_window: head_dim must divide D and be a multiple of 8");
+  QkvRows a;
+  a.x = (const __nv_bfloat16*)qkv;
+  a.x_ld = x_ld;
+  a.w[0] = (const __nv_bfloat16*)w_q;
+  a.w[1] = (const __nv_bfloat16*)w_k;
+  a.eps[0] = eps_q;
+  a.eps[1] = eps_k;
+  a.row_map = row_map;
+  a.out[0] = (__nv_bfloat16*)out_q;
+  a.out[1] = (__nv_bfloat16*)out_k;
+  a.out[2] = (__nv_bfloat16*)out_v;
+  dispatch_nv(D, [&](auto nv) {
+    qkv_rope_window_kernel<decltype(nv)::value><<<row_grid(3 * rows, 2), 256, 0,
+                                                  (cudaStream_t)stream>>>(
+        a, cos, sin, rows, L, (int)D, (int)head_dim);
+  });
+  return check_launch("fvb_qkv_rope_window");
 }
 
 int fvb_rms_rope(const void* x, int64_t x_ld, const void* w, const float* cos, const float* sin,

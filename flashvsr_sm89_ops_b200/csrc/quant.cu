@@ -115,19 +115,30 @@ __global__ void __launch_bounds__(256, kRowBlocksPerSM) quant_row_kernel(
   };
   auto body = [&](int64_t row, uint4* xr) {
     float m = 0.f;
+    // the plain row's amax on packed bf16 pairs (|x| and max are exact on bf16 values;
+    // __hmax2 drops a NaN operand like fmaxf)
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.0f);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       if (j * 32 + lane < nvec) {
-        float f[8];
-        bf16x8_to_f32(xr[j], f);
         if (GELU) {
+          float f[8];
+          bf16x8_to_f32(xr[j], f);
 #pragma unroll
           for (int i = 0; i < 8; ++i) f[i] = gelu_tanh_bf16(f[i]);
           xr[j] = f32_to_bf16x8(f);
-        }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+          for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+        } else {
+          const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xr[j]);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) m2 = __hmax2(m2, __habs2(x2[p]));
+        }
       }
+    }
+    if (!GELU) {
+      const float2 mf = __bfloat1622float2(m2);
+      m = fmaxf(mf.x, mf.y);
     }
     m = warp_max(m);
     const float s = quant_scale_from_amax(m);

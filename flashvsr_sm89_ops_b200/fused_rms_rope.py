@@ -61,6 +61,29 @@ def rms_rope_rows(x2: torch.Tensor, weight: torch.Tensor, cos, sin, L: int, eps:
     return out
 
 
+def qkv_rope_window(qkv: torch.Tensor, w_q: torch.Tensor, w_k: torch.Tensor, cos, sin, L: int,
+                    eps_q: float, eps_k: float, head_dim: int, row_map: torch.Tensor | None,
+                    out_q: torch.Tensor, out_k: torch.Tensor, out_v: torch.Tensor):
+    """q, k and v of the self-attention from the fused projection output qkv [rows, 3D] in
+    one launch: out_q / out_k = RMSNorm + RoPE of the q / k thirds (as rms_rope_rows), out_v
+    = the v third, every row r written to row row_map[r] of its output (each [rows, D])."""
+    _lib.require_cuda(qkv, w_q, w_k)
+    rows, D3 = qkv.shape
+    if qkv.stride(1) != 1 or D3 % 3:
+        raise ValueError("qkv_rope_window: qkv must be [rows, 3D] with unit column stride")
+    D = D3 // 3
+    for o in (out_q, out_k, out_v):
+        if o.shape[0] != rows or o.shape[-1] != D or not o.is_contiguous():
+            raise ValueError("qkv_rope_window: outputs must be contiguous [rows, D]")
+    w_q = w_q.to(torch.bfloat16).contiguous()
+    w_k = w_k.to(torch.bfloat16).contiguous()
+    _lib.call("fvb_qkv_rope_window", _lib.ptr(qkv), qkv.stride(0), _lib.ptr(w_q), _lib.ptr(w_k),
+              _lib.ptr(cos), _lib.ptr(sin), rows, L, D, head_dim, float(eps_q), float(eps_k),
+              _lib.ptr(row_map), _lib.ptr(out_q), _lib.ptr(out_k), _lib.ptr(out_v),
+              _lib.stream_of(qkv))
+    return out_q, out_k, out_v
+
+
 def fused_rms_rope(x: torch.Tensor, weight: torch.Tensor, freqs_cis, eps: float = 1e-6,
                    rope: bool = True, head_dim: int = 128):
     """x [B, L, D] bf16 -> RMSNorm(weight) -> [x RoPE]; freqs_cis complex [L, 1, head_dim/2]."""

@@ -35,7 +35,7 @@ from .fp8_linear import FP8Linear, convert_linears_fp8, fp8_mm
 from .fp8_quant import default_act_mode, quantize_fp8
 from .fused_adaln import (fused_gate_add, fused_ln_modulate, fused_ln_modulate_adaln,
                           gate_add_layer_norm, gate_add_ln_modulate, layer_norm)
-from .fused_rms_rope import freqs_cos_sin, fused_rms_rope, rms_rope_rows
+from .fused_rms_rope import freqs_cos_sin, fused_rms_rope, qkv_rope_window, rms_rope_rows
 
 
 def _FLAG(name, default):
@@ -231,8 +231,6 @@ def _fast_self_attn(self, dit, x, freqs, f, h, w, topk, kv_len, pre_cache_k, pre
         cos, sin = cos.to(x.device), sin.to(x.device)
     r2w, w2r = _row_maps(f, h, w, x.device)
     nq, nk = _unwrap(self.norm_q), _unwrap(self.norm_k)
-    q_w = rms_rope_rows(qkv[:, :D], nq.weight, cos, sin, L, _module_eps(self.norm_q), True, hd,
-                        row_map=r2w)
     seqlen = f // 2
     one_len = (L // 128) // seqlen
     nnew = L // 128
@@ -240,10 +238,12 @@ def _fast_self_attn(self, dit, x, freqs, f, h, w, topk, kv_len, pre_cache_k, pre
     pv = pre_cache_v if pk is not None else None
     ark, ak0, ak1 = _arena_slot(pk, nnew, one_len, D, x.device)
     arv, av0, av1 = _arena_slot(pv, nnew, one_len, D, x.device)
-    # new keys / values land right after the cache: [cache | new] is one contiguous view
-    rms_rope_rows(qkv[:, D:2 * D], nk.weight, cos, sin, L, _module_eps(self.norm_k), True, hd,
-                  out=ark.rows(ak1, ak1 + nnew), row_map=r2w)
-    lcsa.window_partition(qkv[:, 2 * D:], (f, h, w), out=arv.rows(av1, av1 + nnew))
+    # q, and the new keys / values right after the cache ([cache | new] is one contiguous
+    # view), in window order from one launch over the fused projection
+    q_w = torch.empty((L, D), dtype=torch.bfloat16, device=x.device)
+    qkv_rope_window(qkv, nq.weight, nk.weight, cos, sin, L, _module_eps(self.norm_q),
+                    _module_eps(self.norm_k), hd, r2w, q_w, ark.rows(ak1, ak1 + nnew),
+                    arv.rows(av1, av1 + nnew))
     k_w, v_w = ark.rows(ak0, ak1 + nnew), arv.rows(av0, av1 + nnew)
     keep, kpool = _keep_mask(self, dit, q_w, k_w, nh, seqlen, h, w, topk, local_range,
                              pre_cache_k)

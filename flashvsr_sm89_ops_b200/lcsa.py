@@ -201,12 +201,16 @@ def causal_topk_mask(q_w, k_w, nheads, per_row, ratio=0.25, workspace=None, k_po
     if n0 > NK or (n0 and tuple(k_pool_prefix.shape) != (n0, C)):
         raise ValueError(f"causal_topk_mask: k_pool_prefix {tuple(k_pool_prefix.shape)} does not "
                          f"fit {NK} key blocks of {C} channels")
-    aq = block_mean_pool(q_w)
+    aq = torch.empty((NQ, C), dtype=torch.float32, device=q_w.device)
     ak = torch.empty((NK, C), dtype=torch.float32, device=q_w.device)
     if n0:
         ak[:n0].copy_(k_pool_prefix)
-    if n0 < NK:
-        block_mean_pool(k_w.reshape(-1, C)[n0 * BLOCK:], out=ak[n0:])
+    # the query windows and the new key windows pooled in one launch
+    qc = q_w.contiguous()
+    kn = k_w.reshape(-1, C)[n0 * BLOCK:]
+    kn = kn if kn.is_contiguous() else kn.contiguous()
+    _lib.call("fvb_block_mean_pool2", _lib.ptr(qc), NQ, _lib.ptr(kn), NK - n0, C, _lib.ptr(aq),
+              _lib.ptr(ak[n0:]), _lib.stream_of(q_w))
     _lib.call("fvb_causal_topk_pooled", _lib.ptr(aq), _lib.ptr(ak), nheads, NQ, NK, d, per_row,
               float(ratio), _lib.ptr(keep.view(torch.uint8)), _lib.stream_of(q_w))
     return (keep, ak) if return_k_pool else keep

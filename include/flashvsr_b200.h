@@ -151,6 +151,19 @@ FVB_API int fvb_rms_rope(const void* x, int64_t x_ld, const void* w, const float
                  int64_t rows, int64_t L, int64_t D, int64_t head_dim, float eps, int rope,
                  const int32_t* out_row_map, void* out, fvb_stream_t stream);
 
+/* The self-attention's q, k and v in one launch (replaces the two fused_rms_rope calls on
+ * self.q(x) / self.k(x) and the three WindowPartition3D.partition calls of the block,
+ * integrate.py:58-77): from the fused projection qkv [rows, 3D] (row pitch x_ld, 0 -> 3D),
+ *   out_q = fvb_rms_rope(q third, w_q, eps_q, rope), out_k = the same for k with w_k, eps_k,
+ *   out_v = the v third, each input row r written to row out_row_map[r] of its output
+ * (the window order; NULL = identity), bit for bit those three launches.  cos/sin as for
+ * fvb_rms_rope (required). */
+FVB_API int fvb_qkv_rope_window(const void* qkv, int64_t x_ld, const void* w_q, const void* w_k,
+                                const float* cos, const float* sin, int64_t rows, int64_t L,
+                                int64_t D, int64_t head_dim, float eps_q, float eps_k,
+                                const int32_t* out_row_map, void* out_q, void* out_k,
+                                void* out_v, fvb_stream_t stream);
+
 /* ------------------------------------------------- a8: LayerNorm + modulate
  * Replaces fused_ln_modulate(x, scale, shift, eps) (fused_adaln.py:60-71; kernel :22-42):
  *   xn = bf16((x-mean)/sqrt(var+eps));  out = bf16(bf16(xn*bf16(1+scale)) + shift)
@@ -270,6 +283,10 @@ FVB_API int fvb_causal_topk_mask(const void* q_w, const void* k_w, int64_t H, in
  * from pooled aq [NQ, H*d] and ak [NK, H*d] (d % 4 == 0, both 16-byte aligned). */
 FVB_API int fvb_block_mean_pool(const void* x, int64_t nblk, int64_t C, float* out,
                                 fvb_stream_t stream);
+/* Two fvb_block_mean_pool calls in one launch (the step's query windows and its new key
+ * row): out = pool(x [nblk, 128, C]), out2 = pool(x2 [nblk2, 128, C]), bit for bit. */
+FVB_API int fvb_block_mean_pool2(const void* x, int64_t nblk, const void* x2, int64_t nblk2,
+                                 int64_t C, float* out, float* out2, fvb_stream_t stream);
 FVB_API int fvb_causal_topk_pooled(const float* aq, const float* ak, int64_t H, int64_t NQ,
                                    int64_t NK, int64_t d, int64_t per_row, float ratio,
                                    uint8_t* keep, fvb_stream_t stream);

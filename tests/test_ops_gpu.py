@@ -740,3 +740,30 @@ def test_ln_modulate_adaln_equals_add_then_ln_modulate(B, L, D, want_out):
         assert out is None
     assert torch.equal(q8.view(torch.uint8), rq.view(torch.uint8))
     assert torch.equal(qs, rs)
+
+
+@pytest.mark.parametrize("fhw", [(2, 48, 88), (2, 16, 24)])
+def test_qkv_rope_window_equals_three_launches(fhw):
+    """q / k RMSNorm + RoPE and the v window permute of the fused qkv projection in one
+    launch equal the separate rms_rope_rows (q, k) and window_partition (v) launches bit for
+    bit, rows in window order (the 1408x768 step's grid and a small one)."""
+    from flashvsr_sm89_ops_b200 import lcsa
+    from flashvsr_sm89_ops_b200.fused_rms_rope import qkv_rope_window, rms_rope_rows
+    from flashvsr_sm89_ops_b200.integrate import _row_maps
+    f, h, w = fhw
+    L, D, hd = f * h * w, 1536, 128
+    g = gen(61)
+    qkv = (torch.randn(L, 3 * D, generator=g) * 3).to(torch.bfloat16).to(DEV)
+    wq = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16).to(DEV)
+    wk = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16).to(DEV)
+    ang = torch.rand(L, hd // 2, generator=g) * 6.3
+    cos, sin = torch.cos(ang).to(DEV), torch.sin(ang).to(DEV)
+    r2w, _ = _row_maps(f, h, w, torch.device(DEV))
+    oq, ok, ov = (torch.empty(L, D, dtype=torch.bfloat16, device=DEV) for _ in range(3))
+    qkv_rope_window(qkv, wq, wk, cos, sin, L, 1e-6, 2e-6, hd, r2w, oq, ok, ov)
+    rq = rms_rope_rows(qkv[:, :D], wq, cos, sin, L, 1e-6, True, hd, row_map=r2w)
+    rk = rms_rope_rows(qkv[:, D:2 * D], wk, cos, sin, L, 2e-6, True, hd, row_map=r2w)
+    rv = lcsa.window_partition(qkv[:, 2 * D:], (f, h, w))
+    assert torch.equal(oq, rq)
+    assert torch.equal(ok, rk)
+    assert torch.equal(ov, rv)
