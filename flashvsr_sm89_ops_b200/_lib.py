@@ -70,6 +70,8 @@ _SIGS = {
     "fvb_causal_topk_mask": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp]),
     "fvb_block_mean_pool": (_int, [_vp, _i64, _i64, _vp, _vp]),
     "fvb_block_mean_pool2": (_int, [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _vp]),
+    "fvb_causal_topk_pooled_csr": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp,
+                                          _vp, _vp]),
     "fvb_causal_topk_pooled": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp]),
 }
 

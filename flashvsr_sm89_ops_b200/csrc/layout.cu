@@ -279,7 +279,8 @@ __device__ __forceinline__ uint32_t ordered_key(float s) {
 
 __global__ void __launch_bounds__(kTopkThreads) causal_topk_kernel(
     const float* __restrict__ aq, const float* __restrict__ ak, int NQ, int NK, int H, int d,
-    int per_row, float ratio, uint8_t* __restrict__ keep) {
+    int per_row, float ratio, uint8_t* __restrict__ keep, int32_t* __restrict__ sel,
+    int32_t* __restrict__ cnt) {
   extern __shared__ float4 dyn4[];
   const int h = blockIdx.x;
   const int q0 = blockIdx.y * kTopkQ;
@@ -371,10 +372,11 @@ __global__ void __launch_bounds__(kTopkThreads) causal_topk_kernel(
   int gt = 0;
   for (int i = lane; i < npast; i += 32) gt += kq[i] > T;
   const int need = nsel - (int)__reduce_add_sync(0xffffffffu, (unsigned)gt);  // ties to keep
-  uint8_t* kp = keep + ((int64_t)h * NQ + qi) * NK;
+  const int64_t orow = (int64_t)h * NQ + qi;
   const unsigned lt = (1u << lane) - 1u;
-  int eq_before = 0;
-  for (int k0 = 0; k0 < NK; k0 += 32) {
+  // whether key block k0 + lane is kept (every lane calls it for the same k0, in order:
+  // ties are kept in ascending index order up to `need`)
+  auto kept_of = [&](int k0, int& eq_before) {
     const int kj = k0 + lane;
     const bool past = kj < npast;
     const uint32_t kv = past ? kq[kj] : 0u;
@@ -382,9 +384,29 @@ __global__ void __launch_bounds__(kTopkThreads) causal_topk_kernel(
     const unsigned bal = __ballot_sync(0xffffffffu, eq);
     const bool tie_kept = eq && (eq_before + __popc(bal & lt)) < need;
     eq_before += __popc(bal);
-    if (kj < NK) {
-      const int krow = kj / per_row;
-      kp[kj] = (krow == qrow) || (past && nsel > 0 && (kv > T || tie_kept)) ? 1 : 0;
+    return kj < NK && ((kj / per_row == qrow) || (past && nsel > 0 && (kv > T || tie_kept)));
+  };
+  int eq_before = 0, base = 0;
+  int32_t* sr = sel ? sel + orow * NK : nullptr;
+  for (int k0 = 0; k0 < NK; k0 += 32) {
+    const int kj = k0 + lane;
+    const bool kept = kept_of(k0, eq_before);
+    if (keep && kj < NK) keep[orow * NK + kj] = kept ? 1 : 0;
+    if (sr) {  // CSR of the row (fvb_mask_to_csr's order): kept ids ascending ...
+      const unsigned bal = __ballot_sync(0xffffffffu, kept);
+      if (kept) sr[base + __popc(bal & lt)] = kj;
+      base += __popc(bal);
+    }
+  }
+  if (sr) {
+    if (lane == 0) cnt[orow] = base;
+    eq_before = 0;  // ... then the unkept ids ascending (the same decisions, recomputed)
+    for (int k0 = 0; k0 < NK; k0 += 32) {
+      const int kj = k0 + lane;
+      const bool off = !kept_of(k0, eq_before) && kj < NK;
+      const unsigned bal = __ballot_sync(0xffffffffu, off);
+      if (off) sr[base + __popc(bal & lt)] = kj;
+      base += __popc(bal);
     }
   }
 }
@@ -396,7 +418,7 @@ static size_t causal_topk_smem(int64_t NK, int64_t d) {
 
 static int launch_causal_topk(const float* aq, const float* ak, int64_t H, int64_t NQ, int64_t NK,
                               int64_t d, int64_t per_row, float ratio, uint8_t* keep,
-                              cudaStream_t st) {
+                              cudaStream_t st, int32_t* sel = nullptr, int32_t* cnt = nullptr) {
   const size_t smem = causal_topk_smem(NK, d);
   if (smem > 48 * 1024)
     FVB_CUDA_TRY(cudaFuncSetAttribute(causal_topk_kernel,
@@ -404,7 +426,7 @@ static int launch_causal_topk(const float* aq, const float* ak, int64_t H, int64
                  "causal_topk smem");
   causal_topk_kernel<<<dim3((unsigned)H, (unsigned)((NQ + kTopkQ - 1) / kTopkQ)), kTopkThreads,
                        smem, st>>>(aq, ak, (int)NQ, (int)NK, (int)H, (int)d, (int)per_row, ratio,
-                                   keep);
+                                   keep, sel, cnt);
   return check_launch("fvb_causal_topk_mask");
 }
 
@@ -520,6 +542,22 @@ int fvb_block_mean_pool(const void* x, int64_t nblk, int64_t C, float* out, fvb_
   pool_kernel<false><<<dim3((unsigned)nblk, (unsigned)((C + 511) / 512)), 256, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)x, nblk, C, 0, out);
   return check_launch("fvb_block_mean_pool");
+}
+
+int fvb_causal_topk_pooled_csr(const float* aq, const float* ak, int64_t H, int64_t NQ,
+                               int64_t NK, int64_t d, int64_t per_row, float ratio,
+                               uint8_t* keep, int32_t* sel, int32_t* cnt, fvb_stream_t stream) {
+  using namespace fvb;
+  FVB_REQUIRE(H > 0 && NQ > 0 && NK >= NQ && d > 0 && d % 4 == 0,
+              "fvb_causal_topk_pooled_csr: shape");
+  FVB_REQUIRE(per_row > 0 && NQ % per_row == 0 && NK % per_row == 0,
+              "fvb_causal_topk_pooled_csr: blocks per time row must divide NQ and NK");
+  FVB_REQUIRE(aq && ak && sel && cnt && aligned16(aq) && aligned16(ak),
+              "fvb_causal_topk_pooled_csr: pointers");
+  FVB_REQUIRE(NK < (1ll << 31) / H && causal_topk_smem(NK, d) <= 200 * 1024,
+              "fvb_causal_topk_pooled_csr: NK or d too large");
+  return launch_causal_topk(aq, ak, H, NQ, NK, d, per_row, ratio, keep, (cudaStream_t)stream,
+                            sel, cnt);
 }
 
 int fvb_block_mean_pool2(const void* x, int64_t nblk, const void* x2, int64_t nblk2, int64_t C,

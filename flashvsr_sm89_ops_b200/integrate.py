@@ -181,14 +181,16 @@ def _stash_kpool(cache_k, pool):
     cache_k._fvb_kpool = (pool, cache_k._version)
 
 
-def _keep_mask(self, dit, q_w, k_w, nh, seqlen, h, w, topk, local_range, pre_cache_k=None):
-    """Block keep mask; returns (keep, pooled keys or None)."""
+def _keep_mask(self, dit, q_w, k_w, nh, seqlen, h, w, topk, local_range, pre_cache_k=None,
+               csr=False):
+    """Block keep mask; returns (keep, pooled keys or None).  csr (causal rule): the mask's
+    CSR (sel, cnt, NK) from the rule's own launch in place of the mask."""
     D = q_w.shape[-1]
     if getattr(dit, "MASK_RULE", "draft") == "causal":
         per_row = q_w.shape[0] // 128 // seqlen
         return lcsa.causal_topk_mask(q_w, k_w, nh, per_row, getattr(dit, "CAUSAL_RATIO", 0.25),
                                      k_pool_prefix=_cached_kpool(pre_cache_k, D),
-                                     return_k_pool=True)
+                                     return_k_pool=True, csr=csr)
     local = _local_mask(self, dit, h, w, local_range, q_w.device)
     if _FLAG("FS89_FUSED_MASK", "1"):
         return lcsa.draft_block_mask(q_w, k_w, nh, seqlen, local, topk), None
@@ -245,9 +247,13 @@ def _fast_self_attn(self, dit, x, freqs, f, h, w, topk, kv_len, pre_cache_k, pre
                     _module_eps(self.norm_k), hd, r2w, q_w, ark.rows(ak1, ak1 + nnew),
                     arv.rows(av1, av1 + nnew))
     k_w, v_w = ark.rows(ak0, ak1 + nnew), arv.rows(av0, av1 + nnew)
-    keep, kpool = _keep_mask(self, dit, q_w, k_w, nh, seqlen, h, w, topk, local_range,
-                             pre_cache_k)
-    sel, cnt, _ = lcsa.build_csr(keep)
+    if getattr(dit, "MASK_RULE", "draft") == "causal":
+        (sel, cnt, _), kpool = _keep_mask(self, dit, q_w, k_w, nh, seqlen, h, w, topk,
+                                          local_range, pre_cache_k, csr=True)
+    else:
+        keep, kpool = _keep_mask(self, dit, q_w, k_w, nh, seqlen, h, w, topk, local_range,
+                                 pre_cache_k)
+        sel, cnt, _ = lcsa.build_csr(keep)
     o = lcsa.attention_csr(q_w, k_w, v_w, sel, cnt, nh, row_map=w2r)  # raster order
     nkb = k_w.shape[0] // 128
     drop = one_len if (kv_len is not None and nkb // one_len > kv_len) else 0

@@ -177,20 +177,22 @@ def block_mean_pool(x_w, out=None):
 
 
 def causal_topk_mask(q_w, k_w, nheads, per_row, ratio=0.25, workspace=None, k_pool_prefix=None,
-                     return_k_pool=False):
+                     return_k_pool=False, csr=False):
     """Benchmark keep rule on the device: own time row + top floor(ratio*#past) past blocks.
 
     k_pool_prefix: pooled fp32 means of the first key blocks (a streaming caller keeps
     them with its KV cache, since a cached block's mean never changes); only the other
     key blocks are pooled.  return_k_pool: also return the pooled keys [NK, C].
+    csr: return the rule's CSR (sel, cnt, NK), exactly build_csr of the mask, written by
+    the same launch, instead of the mask.
     """
     _lib.require_cuda(q_w, k_w)
     C = q_w.shape[-1]
     NQ = q_w.numel() // (BLOCK * C)
     NK = k_w.numel() // (BLOCK * C)
     d = C // nheads
-    keep = torch.empty((nheads, NQ, NK), dtype=torch.bool, device=q_w.device)
-    if k_pool_prefix is None and not return_k_pool:
+    keep = None if csr else torch.empty((nheads, NQ, NK), dtype=torch.bool, device=q_w.device)
+    if k_pool_prefix is None and not return_k_pool and not csr:
         ws = _workspace(_lib.load().fvb_draft_mask_workspace_bytes(nheads, NQ, NK, d), q_w.device,
                         workspace)
         _lib.call("fvb_causal_topk_mask", _lib.ptr(q_w.contiguous()), _lib.ptr(k_w.contiguous()),
@@ -211,6 +213,14 @@ def causal_topk_mask(q_w, k_w, nheads, per_row, ratio=0.25, workspace=None, k_po
     kn = kn if kn.is_contiguous() else kn.contiguous()
     _lib.call("fvb_block_mean_pool2", _lib.ptr(qc), NQ, _lib.ptr(kn), NK - n0, C, _lib.ptr(aq),
               _lib.ptr(ak[n0:]), _lib.stream_of(q_w))
-    _lib.call("fvb_causal_topk_pooled", _lib.ptr(aq), _lib.ptr(ak), nheads, NQ, NK, d, per_row,
-              float(ratio), _lib.ptr(keep.view(torch.uint8)), _lib.stream_of(q_w))
-    return (keep, ak) if return_k_pool else keep
+    if csr:
+        sel = torch.empty((nheads, NQ, NK), dtype=torch.int32, device=q_w.device)
+        cnt = torch.empty((nheads, NQ), dtype=torch.int32, device=q_w.device)
+        _lib.call("fvb_causal_topk_pooled_csr", _lib.ptr(aq), _lib.ptr(ak), nheads, NQ, NK, d,
+                  per_row, float(ratio), None, _lib.ptr(sel), _lib.ptr(cnt), _lib.stream_of(q_w))
+        res = (sel, cnt, NK)
+    else:
+        _lib.call("fvb_causal_topk_pooled", _lib.ptr(aq), _lib.ptr(ak), nheads, NQ, NK, d,
+                  per_row, float(ratio), _lib.ptr(keep.view(torch.uint8)), _lib.stream_of(q_w))
+        res = keep
+    return (res, ak) if return_k_pool else res

@@ -283,6 +283,13 @@ FVB_API int fvb_causal_topk_mask(const void* q_w, const void* k_w, int64_t H, in
  * from pooled aq [NQ, H*d] and ak [NK, H*d] (d % 4 == 0, both 16-byte aligned). */
 FVB_API int fvb_block_mean_pool(const void* x, int64_t nblk, int64_t C, float* out,
                                 fvb_stream_t stream);
+/* fvb_causal_topk_pooled that also writes the rule's CSR in the same launch: sel
+ * [H, NQ, NK] / cnt [H, NQ] exactly as fvb_mask_to_csr of the keep mask would (kept ids
+ * ascending, then unkept ascending); keep may be NULL (mask not written). */
+FVB_API int fvb_causal_topk_pooled_csr(const float* aq, const float* ak, int64_t H, int64_t NQ,
+                                       int64_t NK, int64_t d, int64_t per_row, float ratio,
+                                       uint8_t* keep, int32_t* sel, int32_t* cnt,
+                                       fvb_stream_t stream);
 /* Two fvb_block_mean_pool calls in one launch (the step's query windows and its new key
  * row): out = pool(x [nblk, 128, C]), out2 = pool(x2 [nblk2, 128, C]), bit for bit. */
 FVB_API int fvb_block_mean_pool2(const void* x, int64_t nblk, const void* x2, int64_t nblk2,

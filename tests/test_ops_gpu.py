@@ -693,6 +693,13 @@ def test_causal_topk_mask_device(nq, nk):
         keep3 = causal_topk_mask(q_w.to(DEV), k_w.to(DEV), H, 66, 0.25,
                                  k_pool_prefix=ak[:npre].clone())
         assert torch.equal(keep3.cpu(), keep)
+    # the CSR written by the rule's own launch (the block path) equals build_csr of the mask
+    from flashvsr_sm89_ops_b200.lcsa import build_csr
+    sel_r, cnt_r, _ = build_csr(keep.to(DEV))
+    (sel, cnt, maxk), _ = causal_topk_mask(q_w.to(DEV), k_w.to(DEV), H, 66, 0.25,
+                                           k_pool_prefix=ak[:npre].clone() if npre else None,
+                                           return_k_pool=True, csr=True)
+    assert maxk == nk and torch.equal(cnt, cnt_r) and torch.equal(sel, sel_r)
 
 
 def test_causal_topk_mask_ties_take_lower_index():
@@ -714,6 +721,11 @@ def test_causal_topk_mask_ties_take_lower_index():
         for i in range(per_row):
             n = int(taken[h, i])
             assert kp[h, i, :n].all() and not kp[h, i, n:].any()
+    # the CSR path resolves the ties the same way
+    from flashvsr_sm89_ops_b200.lcsa import build_csr
+    sel, cnt, _ = causal_topk_mask(q_w.to(DEV), k_w.to(DEV), H, per_row, 0.25, csr=True)
+    sel_r, cnt_r, _ = build_csr(keep.to(DEV))
+    assert torch.equal(sel, sel_r) and torch.equal(cnt, cnt_r)
 
 
 @pytest.mark.parametrize("B,L,D", [(1, 8448, 1536), (2, 37, 256)])
