@@ -214,11 +214,13 @@ __global__ void __launch_bounds__(256) quant_row_long_kernel(const __nv_bfloat16
 
 // Quantisation with a precomputed amax (the second half of fused_gelu_quant_fp8,
 // fp8_ffn.py:57-72, once the GEMM epilogue has reduced the row amax).  One warp per row:
-// the scale and its reciprocal are computed once per row, and each lane keeps six
-// 16-byte loads in flight; 4 blocks of 8 warps are resident per SM.  (A flat grid-stride
+// the scale and its reciprocal are computed once per row, and each lane keeps four
+// 16-byte loads in flight; one resident wave of 4 blocks of 8 warps per SM (measured at
+// the FFN hidden: 4 loads 54.3 us, 6 loads 56.1 us, 8 loads 58.0 us, 10-12 loads with
+// fewer blocks 66-70 us).  (A flat grid-stride
 // loop over the whole matrix spent more time in its 64-bit row = v / (K/8) divides than
 // in memory; a block per row left most threads idle in the row's tail.)
-constexpr int kQaUnroll = 6;
+constexpr int kQaUnroll = 4;
 __global__ void __launch_bounds__(256, 4) quant_with_amax_kernel(
     const uint4* __restrict__ g, int64_t M, int64_t K, const float* __restrict__ amax, int per_row,
     uint2* __restrict__ q, float* __restrict__ scale_out) {
@@ -353,7 +355,7 @@ int fvb_quant_fp8_with_amax(const void* g, int64_t M, int64_t K, const float* am
   FVB_REQUIRE(aligned16(g) && (reinterpret_cast<uintptr_t>(q) & 7u) == 0,
               "fvb_quant_fp8_with_amax: misaligned pointer");
   FVB_REQUIRE(K / 8 <= 0x7fffffff, "fvb_quant_fp8_with_amax: row too long");
-  const int64_t blocks = (M + 7) / 8, cap = (int64_t)sm_count() * 8;
+  const int64_t blocks = (M + 7) / 8, cap = (int64_t)sm_count() * 4;
   quant_with_amax_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, (cudaStream_t)stream>>>(
       (const uint4*)g, M, K, amax, mode == FVB_SCALE_ROW, (uint2*)q, scale_out);
   return check_launch("fvb_quant_fp8_with_amax");
