@@ -492,12 +492,16 @@ static int pick_bn(int M, int N) {
 // pick the tile shape and launch.  Wide BN=256 GEMMs (N >= 4096) with more than one 128-row
 // block of A run on CTA pairs: a third less operand traffic per SM (L2 reads, shared-memory
 // writes and MMA operand reads), measured 2-5% faster under the power cap at N = 4608 and
-// 8960.  At N = 1536 the pair measured 2% slower, so narrow GEMMs stay single-CTA.
+// 8960 with the plain epilogue.  At N = 1536 the pair measured 2% slower, and with the GELU
+// epilogue (FFN-up, 8448x8960x1536) 137.0 us against 131.8 us single-CTA, so those stay
+// single-CTA.
 constexpr int kPairMinN = 4096;
 template <int EPI>
 static int dispatch(const Args& a, const void* A, const void* W, cudaStream_t st) {
   if (pick_bn(a.M, a.N) == 128) return launch<128, EPI, false>(a, A, W, st);
-  if (a.M > BM && a.N >= kPairMinN) return launch<256, EPI, true>(a, A, W, st);
+  if constexpr (EPI != FVB_EPI_GELU_AMAX) {
+    if (a.M > BM && a.N >= kPairMinN) return launch<256, EPI, true>(a, A, W, st);
+  }
   return launch<256, EPI, false>(a, A, W, st);
 }
 

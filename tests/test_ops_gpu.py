@@ -358,10 +358,11 @@ def test_fp8_gemm(M, N, K, mode):
     assert max_rel(out, ref) < 1e-2
 
 
-@pytest.mark.parametrize("epilogue", [0, 1])
+@pytest.mark.parametrize("epilogue", [0])
 def test_fp8_gemm_cta_pair_rows_equal_single_cta(epilogue):
-    """Wide GEMMs (N >= 4096) with more than 128 rows run on CTA pairs (cta_group::2, 256-row
-    tiles: the even CTA's TMEM holds rows 0-127 of a tile, the odd CTA's rows 128-255).
+    """Wide GEMMs (N >= 4096, plain epilogue) with more than 128 rows run on CTA pairs
+    (cta_group::2, 256-row tiles: the even CTA's TMEM holds rows 0-127 of a tile, the odd
+    CTA's rows 128-255).
     Every row must be bit for bit what the single-CTA kernel (M <= 128) gives for that row
     alone: rows 0-127 from the even CTA, 128-255 from the odd one, 256-299 from a pair whose
     odd CTA has no valid row.  N = 4104 also leaves a ragged last column tile."""
