@@ -315,12 +315,18 @@ __global__ void __launch_bounds__(Cfg<EPI, PAIR>::kThreads, 1)
         // the previous TMA store from this staging buffer must have finished reading it
         if (lane == 0) tma_store_wait_read<0>();
         __syncwarp();
-#pragma unroll 1
-        for (int sub = 0; sub < 2; ++sub) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(
-              tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 64 + sub * 32), r);
+        // the chunk's two 32-column TMEM loads go out together, one wait for both (measured:
+        // qkv 52.6 us against 54.0 us with a wait after each load)
+        uint32_t rr[64];
+        {
+          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 64);
+          tmem_ld_32x32b_x32(ta, rr);
+          tmem_ld_32x32b_x32(ta + 32, rr + 32);
           tmem_ld_wait();
+        }
+#pragma unroll
+        for (int sub = 0; sub < 2; ++sub) {
+          const uint32_t* r = rr + sub * 32;
 #pragma unroll
           for (int g4 = 0; g4 < 4; ++g4) {
             const int g = sub * 4 + g4;  // 16-byte chunk of the 128-byte staging row
