@@ -384,16 +384,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
-// contiguous global -> shared copy of `bytes` (a multiple of 16, both addresses 16-byte
-// aligned) whose completion counts on `bar`
-__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes,
-                                             uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x,
                                              int32_t y) {
   asm volatile(
