@@ -367,14 +367,17 @@ __device__ __forceinline__ void unpack_row_f(const uint4* raw, float* f, int lan
 // (mul.rn / add.rn per lane, no contraction), then one bf16 rounding.  rrms =
 // rsqrt(sum(x^2) / D + eps) with the approximate reciprocal square root, as the reference's
 // Triton kernel takes it (tl.rsqrt).
-// One row of RMSNorm (+ RoPE) from the lane's fp32 copy f of the row, written to ov (the
-// output row).  srow: the row's position in the sequence (cos / sin row).
+// One row of RMSNorm (+ RoPE) from the lane's fp32 copy f of the row: input row `row` of a
+// sequence of L rows (cos / sin row row % L), written to output row row_map[row] (or row)
+// of out.  The position and the output row are formed after the row's reduction.
 template <bool ROPE, int NV>
-__device__ __forceinline__ void rms_rope_row(const float* f, int lane, int nvec, float invD,
-                                             float eps, int head_dim, int64_t srow,
+__device__ __forceinline__ void rms_rope_row(const float* f, int lane, int nvec, int D,
+                                             float invD, float eps, int head_dim, int64_t row,
+                                             int64_t L, const int32_t* __restrict__ row_map,
                                              const __nv_bfloat16* __restrict__ w,
                                              const float* __restrict__ cosv,
-                                             const float* __restrict__ sinv, uint4* ov) {
+                                             const float* __restrict__ sinv,
+                                             __nv_bfloat16* __restrict__ out) {
   uint64_t q2 = f2_pack(0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
@@ -390,7 +393,10 @@ __device__ __forceinline__ void rms_rope_row(const float* f, int lane, int nvec,
   f2_unpack(q2, qa, qb);
   const float rrms = rsqrtf(warp_sum(qa + qb) * invD + eps);
   const uint64_t rr = f2_pack(rrms, rrms);
+  const int64_t srow = row % L;
   const int half = head_dim >> 1;
+  const int64_t orow = row_map ? (int64_t)__ldg(row_map + row) : row;
+  uint4* ov = reinterpret_cast<uint4*>(out + orow * D);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const int v = j * 32 + lane;
@@ -449,9 +455,8 @@ __global__ void __launch_bounds__(256, 2) rms_rope_kernel(
   };
   auto prep = [&](int64_t, const uint4* raw, float* f) { unpack_row_f<NV>(raw, f, lane, nvec); };
   auto body = [&](int64_t row, float* f) {
-    const int64_t orow = row_map ? (int64_t)__ldg(row_map + row) : row;
-    rms_rope_row<ROPE, NV>(f, lane, nvec, invD, eps, head_dim, row % L, w, cosv, sinv,
-                           reinterpret_cast<uint4*>(out + orow * D));
+    rms_rope_row<ROPE, NV>(f, lane, nvec, D, invD, eps, head_dim, row, L, row_map, w, cosv,
+                           sinv, out);
   };
   row_pipeline_f<NV, NV>(rows, load, prep, body);
 }
@@ -487,12 +492,12 @@ __global__ void __launch_bounds__(256, 2) qkv_rope_window_kernel(
   auto body = [&](int64_t row, float* f) {
     const int p = (int)(row / R);
     const int64_t r = row - p * R;
-    const int64_t orow = a.row_map ? (int64_t)__ldg(a.row_map + r) : r;
-    uint4* ov = reinterpret_cast<uint4*>(a.out[p] + orow * D);
     if (p < 2) {
-      rms_rope_row<true, NV>(f, lane, nvec, invD, a.eps[p], head_dim, r % L, a.w[p], cosv, sinv,
-                             ov);
+      rms_rope_row<true, NV>(f, lane, nvec, D, invD, a.eps[p], head_dim, r, L, a.row_map,
+                             a.w[p], cosv, sinv, a.out[p]);
     } else {
+      const int64_t orow = a.row_map ? (int64_t)__ldg(a.row_map + r) : r;
+      uint4* ov = reinterpret_cast<uint4*>(a.out[p] + orow * D);
 #pragma unroll
       for (int j = 0; j < NV; ++j)
         if (j * 32 + lane < nvec) ov[j * 32 + lane] = f32_to_bf16x8(f + 8 * j);  // exact
