@@ -161,6 +161,13 @@ __global__ void __launch_bounds__(256, kRowBlocksPerSM) quant_row_kernel(
 // One warp per row, rows strided over a persistent grid.  GELU (GELU(tanh) -> e4m3 of
 // fp8_ffn.py:57-72) goes through the block's shared table of the exact function of the
 // 16-bit input (gelu_bf16_bits), built once per block.
+// GELU's row amax without GELU in the first pass: GELU rounded to bf16 is non-decreasing
+// for x >= 0 (checked on the block's table; if it were not, every row takes the exact pass),
+// and every negative input has |GELU(x)| <= neg_max, the largest negative-half entry of the
+// table (~0.17, at x ~ -0.75; inputs outside the table give |GELU| < 2^-10).  So when
+// GELU(row max) >= neg_max, the amax of |GELU| over the row is GELU(row max), and the first
+// pass is a packed bf16 max of the raw row; otherwise the row takes the exact pass (GELU of
+// every element).  NaN inputs are dropped from the amax either way, like fmaxf.
 template <bool GELU>
 __device__ __forceinline__ void load8_lut(const uint4* src, int64_t v, const uint16_t* lut,
                                           float* f) {
@@ -183,8 +190,22 @@ __global__ void __launch_bounds__(256) quant_row_long_kernel(const __nv_bfloat16
                                                              uint8_t* __restrict__ q,
                                                              float* __restrict__ scale_out) {
   __shared__ uint16_t lut[GELU ? 2 * kGeluRange : 1];
+  __shared__ uint32_t neg_max, not_mono;
   if (GELU) {
+    if (threadIdx.x == 0) neg_max = not_mono = 0u;
     gelu_table_fill(lut, threadIdx.x, blockDim.x);
+    __syncthreads();
+    uint32_t nm = 0u, bad = 0u;
+    for (uint32_t i = threadIdx.x; i < kGeluRange; i += blockDim.x) {
+      nm = max(nm, (uint32_t)lut[kGeluRange + i] & 0x7FFFu);
+      if (i + 1 < kGeluRange && lut[i + 1] < lut[i]) bad = 1u;  // positive half, ascending x
+    }
+    // the table's ends meet the rules outside it: 0.5 x below, x above
+    if (threadIdx.x == 0 && (lut[0] < bf16_bits_rn(0.5f * __uint_as_float((kGeluLo - 1u) << 16)) ||
+                             lut[kGeluRange - 1] > kGeluLo + kGeluRange))
+      bad = 1u;
+    if (nm) atomicMax(&neg_max, nm);
+    if (bad) atomicOr(&not_mono, 1u);
     __syncthreads();
   }
   const int lane = threadIdx.x & 31;
@@ -194,13 +215,34 @@ __global__ void __launch_bounds__(256) quant_row_long_kernel(const __nv_bfloat16
     const uint4* xv = reinterpret_cast<const uint4*>(x + row * K);
     uint2* qv = reinterpret_cast<uint2*>(q + row * K);
     float m = 0.f;
-    for (int64_t v = lane; v < nvec; v += 32) {
-      float f[8];
-      load8_lut<GELU>(xv, v, lut, f);
+    bool exact = true;
+    if (GELU && not_mono == 0u) {
+      // packed bf16 max of the raw row (__hmax2 drops a NaN operand)
+      __nv_bfloat162 mx2 = __halves2bfloat162(__ushort_as_bfloat16((unsigned short)0xFF80u),
+                                               __ushort_as_bfloat16((unsigned short)0xFF80u));
+      for (int64_t v = lane; v < nvec; v += 32) {
+        const uint4 u = __ldg(xv + v);
+        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+        for (int p = 0; p < 4; ++p) mx2 = __hmax2(mx2, x2[p]);
+      }
+      const float2 mf = __bfloat1622float2(mx2);
+      const float xmax = warp_max(fmaxf(mf.x, mf.y));
+      const uint32_t gb = gelu_bf16_bits(bf16_bits_rn(xmax), lut);
+      if (xmax > 0.f && (gb & 0x7FFFu) >= neg_max && (gb & 0x7FFFu) <= 0x7F80u) {
+        m = __uint_as_float(gb << 16);
+        exact = false;
+      }
     }
-    m = warp_max(m);
+    if (exact) {
+      for (int64_t v = lane; v < nvec; v += 32) {
+        float f[8];
+        load8_lut<GELU>(xv, v, lut, f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+      }
+      m = warp_max(m);
+    }
     const float s = quant_scale_from_amax(m);
     const float rs = __frcp_rn(s);
     for (int64_t v = lane; v < nvec; v += 32) {

@@ -184,6 +184,10 @@ def timing(R, dev):
                           _lib.FVB_SCALE_ROW, _lib.ptr(q8), _lib.ptr(s8), _lib.stream_of(hdn)),
         "reference: 2 passes (GELU+amax, GELU+quant); pack: GELU and amax are in the GEMM-1 "
         "epilogue, this is the one remaining pass")
+    from flashvsr_sm89_ops_b200.fp8_quant import fused_gelu_quant_fp8 as b_gelu_quant
+    add("fused_gelu_quant_fp8 (standalone, per token)", f"[{L},{FF}]",
+        lambda: R.fused_gelu_quant_fp8(hdn), lambda: b_gelu_quant(hdn, "token"),
+        "both sides apply GELU, reduce the amax and quantise; the reference per tensor")
     w = (1 + 0.1 * torch.randn(D, generator=gd, device=dev)).to(torch.bfloat16)
     fr = _freqs(L, 3).to(dev)
     x3 = x.view(1, L, D)

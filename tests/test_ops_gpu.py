@@ -178,13 +178,15 @@ def test_gelu_quant_matches_gpu_eager_bitexact(mode):
     assert d.max().item() <= 1 and (d > 0).float().mean().item() < 1e-3
 
 
-@pytest.mark.parametrize("rows", ["every_bf16", "step"])
+@pytest.mark.parametrize("rows", ["every_bf16", "step", "small_max"])
 def test_gelu_quant_long_rows_bitexact(rows):
-    """Per-token GELU -> FP8 on rows longer than 2048 (the FFN hidden, 8960 wide) runs one
-    warp per row over a shared-memory copy of the row with GELU from a table.  Codes and
-    scales must equal quantize_fp8(F.gelu(h)) on the GPU bit for bit: for every bf16 input
-    value (NaN patterns zeroed; rows holding +-inf included) and at the step's 8448 rows,
-    where each warp takes several rows in turn."""
+    """Per-token GELU -> FP8 on rows longer than 2048 (the FFN hidden, 8960 wide): one warp
+    per row, GELU from a shared table, the row amax taken as GELU(row max) when that is at
+    least every negative input's |GELU|, else from GELU of every element.  Codes and scales
+    must equal quantize_fp8(F.gelu(h)) on the GPU bit for bit: for every bf16 input value
+    (NaN patterns zeroed; rows holding +-inf included), at the step's 8448 rows (each warp
+    takes several rows in turn), and on rows whose maximum is too small for the shortcut
+    (values in [-4, 0.25], an all-negative row, a row peaking near the bound)."""
     from flashvsr_sm89_ops_b200 import quantize_fp8
     from flashvsr_sm89_ops_b200.fp8_quant import fused_gelu_quant_fp8
     K = 8960
@@ -193,8 +195,18 @@ def test_gelu_quant_long_rows_bitexact(rows):
         x = torch.where(torch.isnan(x), torch.zeros_like(x), x)
         x = torch.cat([x, torch.zeros(8 * K - x.numel(), dtype=torch.bfloat16)]).view(8, K)
         h = x[torch.randperm(8, generator=gen(8))].contiguous().to(DEV)
-    else:
+    elif rows == "step":
         h = (torch.randn(8448, K, generator=gen(9)) * 2).to(torch.bfloat16).to(DEV)
+    else:
+        g = gen(10)
+        h = torch.rand(16, K, generator=g) * 4.25 - 4.0       # max 0.25: GELU 0.149 < ~0.17
+        h[1] = -torch.rand(K, generator=g) * 3 - 0.01         # all negative
+        h[2, :] = -0.75                                       # |GELU| at its negative peak,
+        h[2, 7] = 0.279296875                                 # tied by GELU of this peak
+        h[3, :] = -0.75
+        h[3, 7] = 0.27734375                                  # one bf16 step below: the
+        #                                                       negative inputs set the amax
+        h = h.to(torch.bfloat16).to(DEV)
     q, s = fused_gelu_quant_fp8(h, "token")
     qe, se = quantize_fp8(F.gelu(h, approximate="tanh"), "token")
     assert torch.equal(s, se)
