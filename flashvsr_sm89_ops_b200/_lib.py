@@ -122,8 +122,10 @@ def _raise(rc: int, name: str):
 
 def _kernels_per_call(name: str, args) -> int:
     """How many of this library's kernels one C-ABI call launches."""
-    if name in ("fvb_quant_fp8", "fvb_gelu_quant_fp8"):
+    if name == "fvb_quant_fp8":
         return 2 if args[5] == FVB_SCALE_TENSOR else 1
+    if name == "fvb_gelu_quant_fp8":
+        return 3 if args[5] == FVB_SCALE_TENSOR else 1
     if name in ("fvb_fp8_ffn", "fvb_fp8_ffn_residual"):
         return 3
     if name == "fvb_draft_block_mask":

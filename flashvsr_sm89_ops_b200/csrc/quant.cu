@@ -96,6 +96,115 @@ __global__ void __launch_bounds__(256) quant_tensor_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// per-tensor GELU -> e4m3 (fused_gelu_quant_fp8's default mode) in three launches:
+//   1. the raw maximum of h (no GELU); block 0 also evaluates GELU on every bf16 input of the
+//      table range to get neg_max (the largest |GELU| of a negative input) and to check that
+//      GELU is non-decreasing on the positive ones;
+//   2. amax = GELU(max h) when max h > 0, GELU(max h) >= neg_max and the check held (GELU is
+//      non-decreasing for x >= 0 and every negative input's |GELU| is at most neg_max);
+//      otherwise every block takes GELU of its elements and the exact amax is reduced;
+//   3. quantise, GELU through the block's shared table.
+// Workspace (floats): [0] amax, [1] max h as an order-preserving uint32 key, [2] neg_max,
+// [3] nonzero when the check failed.  NaN inputs are dropped from the maxima like fmaxf.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float order_key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+__global__ void __launch_bounds__(256) gelu_rawmax_kernel(const uint4* __restrict__ x, int64_t nvec,
+                                                          const __nv_bfloat16* __restrict__ xs,
+                                                          int64_t n, float* __restrict__ ws) {
+  float m = -INFINITY;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    float f[8];
+    bf16x8_to_f32(__ldg(x + v), f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, f[i]);
+  }
+  if (blockIdx.x == 0) {
+    for (int64_t i = nvec * 8 + threadIdx.x; i < n; i += blockDim.x)
+      m = fmaxf(m, __bfloat162float(xs[i]));
+    // the table range, both signs: neg_max and the positive side's order
+    float nm = 0.f;
+    uint32_t bad = 0u;
+    for (uint32_t i = threadIdx.x; i < kGeluRange; i += blockDim.x) {
+      const float xn = __uint_as_float((0x8000u | (kGeluLo + i)) << 16);
+      nm = fmaxf(nm, fabsf(gelu_tanh_bf16(xn)));
+      const float xp = __uint_as_float((kGeluLo + i) << 16);
+      const float xp1 = __uint_as_float((kGeluLo + i + 1u) << 16);  // i + 1 == range: x = 16
+      const float gp1 = i + 1u < kGeluRange ? gelu_tanh_bf16(xp1) : xp1;
+      if (gelu_tanh_bf16(xp) > gp1) bad = 1u;
+    }
+    nm = warp_max(nm);
+    if ((threadIdx.x & 31) == 0) atomic_max_nonneg(ws + 2, nm);
+    if (bad) atomicOr(reinterpret_cast<unsigned int*>(ws + 3), 1u);
+  }
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0 && m == m)
+    atomicMax(reinterpret_cast<unsigned int*>(ws + 1), order_key(m));
+}
+
+__global__ void __launch_bounds__(256) gelu_amax_kernel(const uint4* __restrict__ x, int64_t nvec,
+                                                        const __nv_bfloat16* __restrict__ xs,
+                                                        int64_t n, float* __restrict__ ws) {
+  const uint32_t key = *reinterpret_cast<const volatile uint32_t*>(ws + 1);
+  const float xmax = key ? order_key_value(key) : -INFINITY;
+  const float g = gelu_tanh_bf16(xmax);
+  const bool bad = *reinterpret_cast<const volatile uint32_t*>(ws + 3) != 0u;
+  if (!bad && xmax > 0.f && g >= ws[2]) {  // the shortcut holds (g may be +inf)
+    if (blockIdx.x == 0 && threadIdx.x == 0) ws[0] = g;
+    return;
+  }
+  // exact: |GELU| of every element
+  float m = 0.f;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    float f[8];
+    load8<true>(x, v, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(f[i]));
+  }
+  if (blockIdx.x == 0)
+    for (int64_t i = nvec * 8 + threadIdx.x; i < n; i += blockDim.x)
+      m = fmaxf(m, fabsf(gelu_tanh_bf16(__bfloat162float(xs[i]))));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) atomic_max_nonneg(ws, m);
+}
+
+__global__ void __launch_bounds__(256) gelu_quant_tensor_kernel(
+    const uint4* __restrict__ x, int64_t nvec, const __nv_bfloat16* __restrict__ xs, int64_t n,
+    const float* __restrict__ amax_p, uint2* __restrict__ q, uint8_t* __restrict__ qs,
+    float* __restrict__ scale_out) {
+  __shared__ uint16_t lut[2 * kGeluRange];
+  gelu_table_fill(lut, threadIdx.x, blockDim.x);
+  __syncthreads();
+  const float amax = *amax_p;
+  const float s = quant_scale_from_amax(amax);
+  const float rs = __frcp_rn(s);
+  if (blockIdx.x == 0 && threadIdx.x == 0) scale_out[0] = returned_scale(amax);
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 u = __ldg(x + v);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(gelu_bf16_bits(w[i] & 0xFFFFu, lut) << 16);
+      f[2 * i + 1] = __uint_as_float(gelu_bf16_bits(w[i] >> 16, lut) << 16);
+    }
+    q[v] = quant8(f, s, rs);
+  }
+  if (blockIdx.x == 0)
+    for (int64_t i = nvec * 8 + threadIdx.x; i < n; i += blockDim.x)
+      qs[i] = f32_to_e4m3(__fdiv_rn(gelu_tanh_bf16(__bfloat162float(xs[i])), s));
+}
+
+// ---------------------------------------------------------------------------
 // per-token: one warp per row
 // ---------------------------------------------------------------------------
 // K <= 2048: the row lives in registers (NV 16-byte vectors per lane), two rows per warp in
@@ -353,15 +462,30 @@ static int quant_impl(const void* x, int64_t M, int64_t K, void* q, float* scale
   FVB_REQUIRE(workspace != nullptr, "%s: per-tensor mode needs a workspace", name);
   FVB_REQUIRE((reinterpret_cast<uintptr_t>(q) & 7u) == 0, "%s: q not 8-byte aligned", name);
   float* amax = static_cast<float*>(workspace);
-  FVB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(float), st), name);
+  FVB_CUDA_TRY(cudaMemsetAsync(amax, 0, (GELU ? 4 : 1) * sizeof(float), st), name);
   const int64_t nvec = n >> 3;
   const int g = grid_for(nvec > 0 ? nvec : 1, 256);
-  absmax_kernel<GELU><<<g, 256, 0, st>>>((const uint4*)x, nvec, (const __nv_bfloat16*)x, n, amax);
-  int rc = check_launch(name);
-  if (rc) return rc;
-  quant_tensor_kernel<GELU><<<g, 256, 0, st>>>((const uint4*)x, nvec, (const __nv_bfloat16*)x, n,
-                                               amax, (uint2*)q, (uint8_t*)q, scale_out);
-  return check_launch(name);
+  if constexpr (GELU) {
+    gelu_rawmax_kernel<<<g, 256, 0, st>>>((const uint4*)x, nvec, (const __nv_bfloat16*)x, n, amax);
+    int rc = check_launch(name);
+    if (rc) return rc;
+    gelu_amax_kernel<<<g, 256, 0, st>>>((const uint4*)x, nvec, (const __nv_bfloat16*)x, n, amax);
+    rc = check_launch(name);
+    if (rc) return rc;
+    const int64_t cap = (int64_t)sm_count() * 4;
+    gelu_quant_tensor_kernel<<<(unsigned)(g < cap ? g : cap), 256, 0, st>>>(
+        (const uint4*)x, nvec, (const __nv_bfloat16*)x, n, amax, (uint2*)q, (uint8_t*)q,
+        scale_out);
+    return check_launch(name);
+  } else {
+    absmax_kernel<GELU><<<g, 256, 0, st>>>((const uint4*)x, nvec, (const __nv_bfloat16*)x, n,
+                                           amax);
+    int rc = check_launch(name);
+    if (rc) return rc;
+    quant_tensor_kernel<GELU><<<g, 256, 0, st>>>((const uint4*)x, nvec, (const __nv_bfloat16*)x, n,
+                                                 amax, (uint2*)q, (uint8_t*)q, scale_out);
+    return check_launch(name);
+  }
 }
 
 }  // namespace fvb

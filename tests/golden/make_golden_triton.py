@@ -185,9 +185,12 @@ def timing(R, dev):
         "reference: 2 passes (GELU+amax, GELU+quant); pack: GELU and amax are in the GEMM-1 "
         "epilogue, this is the one remaining pass")
     from flashvsr_sm89_ops_b200.fp8_quant import fused_gelu_quant_fp8 as b_gelu_quant
-    add("fused_gelu_quant_fp8 (standalone, per token)", f"[{L},{FF}]",
+    add("fused_gelu_quant_fp8 (standalone, per tensor)", f"[{L},{FF}]",
+        lambda: R.fused_gelu_quant_fp8(hdn), lambda: b_gelu_quant(hdn, "tensor"),
+        "both sides apply GELU, reduce the amax and quantise")
+    add("fused_gelu_quant_fp8 (standalone, pack per token)", f"[{L},{FF}]",
         lambda: R.fused_gelu_quant_fp8(hdn), lambda: b_gelu_quant(hdn, "token"),
-        "both sides apply GELU, reduce the amax and quantise; the reference per tensor")
+        "the reference per tensor")
     w = (1 + 0.1 * torch.randn(D, generator=gd, device=dev)).to(torch.bfloat16)
     fr = _freqs(L, 3).to(dev)
     x3 = x.view(1, L, D)

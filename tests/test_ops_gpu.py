@@ -214,6 +214,36 @@ def test_gelu_quant_long_rows_bitexact(rows):
     assert neq == 0, f"{neq} codes differ from quantize_fp8(F.gelu(h))"
 
 
+@pytest.mark.parametrize("case", ["every_bf16", "small_max", "all_negative", "tie", "below_tie",
+                                  "ragged"])
+def test_gelu_quant_tensor_mode_bitexact(case):
+    """Per-tensor GELU -> FP8 (the reference's default mode) takes the amax as GELU(max h) when
+    that bounds every negative input's |GELU|, else from GELU of every element; both paths
+    and a ragged tail must give quantize_fp8(F.gelu(h), "tensor") on the GPU bit for bit."""
+    from flashvsr_sm89_ops_b200 import quantize_fp8
+    from flashvsr_sm89_ops_b200.fp8_quant import fused_gelu_quant_fp8
+    g = gen(11)
+    if case == "every_bf16":
+        h = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+        h = torch.where(torch.isnan(h), torch.zeros_like(h), h)
+        h = h[torch.isfinite(h)]  # the finite values: GELU(+inf) would make the amax inf
+        h = torch.cat([h, torch.zeros(-h.numel() % 64, dtype=h.dtype)]).view(-1, 64)
+    elif case == "small_max":
+        h = torch.rand(64, 1024, generator=g) * 4.25 - 4.0
+    elif case == "all_negative":
+        h = -torch.rand(64, 1024, generator=g) * 3 - 0.01
+    elif case in ("tie", "below_tie"):
+        h = torch.full((64, 1024), -0.75)
+        h[5, 9] = 0.279296875 if case == "tie" else 0.27734375
+    else:
+        h = torch.randn(7, 13, generator=g) * 3
+    h = h.to(torch.bfloat16).to(DEV)
+    q, s = fused_gelu_quant_fp8(h, "tensor")
+    qe, se = quantize_fp8(F.gelu(h, approximate="tanh"), "tensor")
+    assert torch.equal(s, se)
+    assert torch.equal(q.view(torch.uint8), qe.view(torch.uint8))
+
+
 # ----------------------------------------------------------------------------- AdaLN
 def test_gate_add_bitwise():
     from flashvsr_sm89_ops_b200 import fused_gate_add
