@@ -147,6 +147,29 @@ def test_quantize_fp8_near_midpoints():
     assert torch.equal(q2.view(torch.uint8).cpu(), qr.view(torch.uint8))
 
 
+@pytest.mark.parametrize("M,K", [(1, 8), (5, 8960), (1000, 8960), (297, 1536), (6000, 1536),
+                                 (8448, 8960), (3, 12288), (7, 12296)])
+@pytest.mark.parametrize("mode", ["token", "tensor"])
+def test_quant_with_amax_shapes_bitexact(M, K, mode):
+    """The quantiser given the amax (the FFN's hidden quantisation): fewer rows than warps,
+    a few rows per warp and the step's 8448 x 8960, row lengths from one vector to 12296
+    (a ragged last round of a lane's four loads), both scale modes, against the oracle."""
+    from flashvsr_sm89_ops_b200 import _lib
+    x = (torch.randn(M, K, generator=gen(M + K)) * 2).to(torch.bfloat16)
+    qr, sr = O.quantize_fp8(x, mode)
+    xd = x.to(DEV)
+    a = xd.float().abs()
+    amax = (a.amax(dim=1) if mode == "token" else a.amax().reshape(1)).contiguous()
+    q = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=DEV)
+    s = torch.empty(M if mode == "token" else 1, dtype=torch.float32, device=DEV)
+    code = _lib.FVB_SCALE_ROW if mode == "token" else _lib.FVB_SCALE_TENSOR
+    _lib.call("fvb_quant_fp8_with_amax", _lib.ptr(xd), M, K, _lib.ptr(amax), code, _lib.ptr(q),
+              _lib.ptr(s), _lib.stream_of(xd))
+    assert torch.equal(q.view(torch.uint8).cpu(), qr.view(torch.uint8))
+    assert torch.equal(s.cpu().reshape(-1), sr.float().reshape(-1))
+    assert _lib.device_error() == 0
+
+
 def test_quantize_fp8_tensor_ragged_and_empty():
     from flashvsr_sm89_ops_b200 import quantize_fp8
     x = torch.randn(7, 13, generator=gen(3)).to(torch.bfloat16)
