@@ -51,10 +51,19 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--blocks", type=int, default=BLOCKS)
     p.add_argument("--no-graph", action="store_true")
-    p.add_argument("--only", default=None, choices=sorted(ONLY_KERNELS),
-                   help="time one kernel of the step in isolation at the step's shape "
-                        "(profiling / per-kernel roofline); prints one JSON line")
-    return p.parse_args()
+    p.add_argument("--only", default=None,
+                   help="time kernels of the step in isolation at the step's shape "
+                        "(profiling / per-kernel roofline): one name of ONLY_KERNELS or a "
+                        "comma-separated list; prints one JSON line per kernel")
+    p.add_argument("--graph", action="store_true",
+                   help="with --only: capture the timed calls in one CUDA graph and time its "
+                        "replay, so host-side call overhead is not in the per-launch time")
+    a = p.parse_args()
+    if a.only is not None:
+        bad = [k for k in a.only.split(",") if k not in ONLY_KERNELS]
+        if bad:
+            p.error(f"--only: unknown kernel(s) {bad}; choose from {sorted(ONLY_KERNELS)}")
+    return a
 
 
 # kernels of one block at the step's shape, runnable in isolation (--only)
@@ -67,6 +76,41 @@ L2_BYTES = 126 << 20
 
 
 def run_only(args, local_rank):
+    """Run each kernel named by --only (comma-separated) in turn, in this process."""
+    import copy
+    for name in args.only.split(","):
+        one = copy.copy(args)
+        one.only = name
+        _run_only_one(one, local_rank)
+
+
+def _time_graph(fn, steps, dev):
+    """Per-launch ms of `steps` calls of fn captured in one CUDA graph, replayed once to warm
+    and once timed with CUDA events on the launching stream."""
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(steps):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    del graph
+    return ms
+
+
+def _run_only_one(args, local_rank):
     """Run one kernel class K times at the workload's shapes; report time and roofline.
 
     Memory-bound kernels cycle through enough independent input sets to cover three times
@@ -171,7 +215,8 @@ def run_only(args, local_rank):
             q = torch.empty(L, FFN, dtype=torch.float8_e4m3fn, device=dev)
             sc = torch.empty(L, device=dev)
             return lambda: _lib.call("fvb_quant_fp8_with_amax", _lib.ptr(h), L, FFN, _lib.ptr(amax),
-                                     _lib.FVB_SCALE_ROW, _lib.ptr(q), _lib.ptr(sc), st)
+                                     _lib.FVB_SCALE_ROW, _lib.ptr(q), _lib.ptr(sc),
+                                     _lib.stream_of(h))
         work = L * FFN * 3 + L * 8
         fn = rotating(make, work)
     elif args.only == "quant_token":
@@ -258,6 +303,9 @@ def run_only(args, local_rank):
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / args.steps
+    ms_eager = ms
+    if args.graph:
+        ms = _time_graph(fn, args.steps, dev)
     fp8 = args.only in ("gemm_qkv", "gemm_o", "gemm_up", "gemm_up_gelu", "gemm_down", "ffn") or \
         args.only.startswith("cublaslt_")
     if bound == "tensor" and fp8:
@@ -269,7 +317,8 @@ def run_only(args, local_rank):
         ach, peak, unit = work / (ms / 1e3) / 1e9, float(peaks.get("hbm_gbs", 6650.0)), "GB/s"
     print(json.dumps({"only": args.only, "ms_per_launch": ms, "work_per_launch": work, "bound": bound,
                       "achieved": ach, "peak": peak, "unit": unit, "frac": ach / peak,
-                      "peak_kind": kind}))
+                      "peak_kind": kind, "timing": "cuda_graph" if args.graph else "eager",
+                      "ms_per_launch_eager": ms_eager}))
 
 
 def measure_fp8_peak(dev):

@@ -176,18 +176,18 @@ __device__ __forceinline__ uint2 e4m3_codes8(const float* f, float s, float rs) 
   const uint64_t lo2 = f2_pack(rs * 0.99999904632568359375f, rs * 0.99999904632568359375f);
   const uint64_t hi2 = f2_pack(rs * 1.00000095367431640625f, rs * 1.00000095367431640625f);
   uint32_t c[4];
-  bool exact = false;
+  uint32_t diff = 0;  // OR of (lo ^ hi) over the pairs: one 3-input logic op per pair
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint64_t x2 = f2_pack(f[2 * i], f[2 * i + 1]);
     float a0, a1, b0, b1;
     f2_unpack(f2_mul(x2, lo2), a0, a1);
     f2_unpack(f2_mul(x2, hi2), b0, b1);
-    const uint16_t lo = f32x2_to_e4m3x2(a0, a1), hi = f32x2_to_e4m3x2(b0, b1);
-    exact |= lo != hi;
+    const uint32_t lo = f32x2_to_e4m3x2(a0, a1), hi = f32x2_to_e4m3x2(b0, b1);
+    diff |= lo ^ hi;
     c[i] = lo;
   }
-  if (exact) return e4m3x8_exact(f[0], f[1], f[2], f[3], f[4], f[5], f[6], f[7], s);
+  if (diff != 0) return e4m3x8_exact(f[0], f[1], f[2], f[3], f[4], f[5], f[6], f[7], s);
   return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
 }
 
