@@ -65,6 +65,7 @@ _SIGS = {
     "fvb_mask_to_csr": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "fvb_bsa_fwd": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp]),
     "fvb_window_partition": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _int, _vp, _vp]),
+    "fvb_copy_window_h2d": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
     "fvb_draft_mask_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "fvb_draft_block_mask": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "fvb_causal_topk_mask": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp, _vp, _vp]),
@@ -132,8 +133,8 @@ def _kernels_per_call(name: str, args) -> int:
         return 4
     if name == "fvb_causal_topk_mask":
         return 3
-    if name in ("fvb_device_error", "fvb_abi_version", "fvb_last_error"):
-        return 0
+    if name in ("fvb_device_error", "fvb_abi_version", "fvb_last_error", "fvb_copy_window_h2d"):
+        return 0  # no kernel (fvb_copy_window_h2d is a copy-engine transfer)
     return 1
 
 

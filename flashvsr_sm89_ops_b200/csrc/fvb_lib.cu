@@ -7,3 +7,4 @@
 #include "gemm_fp8.cu"
 #include "bsa.cu"
 #include "noalloc.cu"
+#include "crop_copy.cu"

@@ -149,36 +149,45 @@ def _dist_info(group):
 
 
 class _Staging:
-    """Two pinned host buffers and two device buffers for one device and dtype, with the
-    events that order their reuse, kept across render_tiled calls: pinning a few hundred MB
-    of host memory takes a large fraction of a second, which a fresh allocation per call
-    would add to every render.  Calls on one device share them, so render_tiled calls on
-    the same device must not run concurrently from several host threads."""
+    """Two device buffers (and, for a pageable host video, two pinned host buffers) for one
+    device and dtype, with the events that order their reuse, kept across render_tiled
+    calls: pinning a few hundred MB of host memory takes a large fraction of a second, which
+    a fresh allocation per call would add to every render.  Calls on one device share them,
+    so render_tiled calls on the same device must not run concurrently from several host
+    threads."""
 
-    def __init__(self, device, dtype, numel):
-        self.stage = [torch.empty(numel, dtype=dtype, pin_memory=True) for _ in range(2)]
+    def __init__(self, device, dtype, numel, host=True):
+        self.stage = [torch.empty(numel, dtype=dtype, pin_memory=True)
+                      for _ in range(2)] if host else []
         self.dev = [torch.empty(numel, dtype=dtype, device=device) for _ in range(2)]
-        self.up_done = [None, None]    # upload from stage b finished (host may refill it)
+        self.up_done = [None, None]    # upload into device buffer b (from stage b) finished
         self.used = [None, None]       # render of the tile in device buffer b finished
 
     def numel(self):
-        return self.stage[0].numel()
+        return self.dev[0].numel()
 
 
 _STAGING = {}
 
 
-def _staging_for(device, dtype, numel):
-    key = (str(torch.device(device)), dtype)
+def _staging_for(device, dtype, numel, host=True):
+    key = (str(torch.device(device)), dtype, host)
     st = _STAGING.get(key)
     if st is None or st.numel() < numel:
         if st is not None:  # the old buffers may still feed work in flight
             for ev in st.up_done + st.used:
                 if ev is not None:
                     ev.synchronize()
-        st = _Staging(device, dtype, numel)
+        st = _Staging(device, dtype, numel, host)
         _STAGING[key] = st
     return st
+
+
+def _dma_source(lq, device):
+    """A pinned, contiguous host video: crops go to the device as one strided copy-engine
+    transfer each (fvb_copy_window_h2d), with no host-side packing."""
+    return (torch.device(device).type == "cuda" and lq.device.type == "cpu"
+            and lq.is_pinned() and lq.is_contiguous())
 
 
 def _crop_numel(lq, tiles, order):
@@ -201,7 +210,7 @@ def reserve_staging(lq_video, *, overlap=OVERLAP, tile_target=TILE_TARGET,
     world, rank = _dist_info(group)
     n = _crop_numel(lq, tiles, assign_tiles(len(tiles), world, rank))
     if n:
-        _staging_for(device, lq.dtype, n)
+        _staging_for(device, lq.dtype, n, host=not _dma_source(lq, device))
 
 
 def release_staging():
@@ -223,17 +232,29 @@ class _TileLoader:
     device buffers rotate (kept across calls, see _Staging); the side stream reuses a device
     buffer only after the render of the tile that used it (an event recorded after its
     blend).  A video already on the device is cropped there.
+    A pinned contiguous host video needs no packing: the side stream copies each crop
+    straight from it with one strided copy-engine transfer (crop k+1 is queued when tile k
+    starts), so no host thread touches the pixels and ranks sharing a host do not compete
+    for its memory bandwidth.
     """
 
     def __init__(self, lq, tiles, order, device):
         device = torch.device(device)
         self.lq, self.tiles, self.order, self.device = lq, tiles, list(order), device
         self.direct = lq.device == device or device.type != "cuda"
+        self.dma = False
         if self.direct:
             return
         from concurrent.futures import ThreadPoolExecutor
-        self.st = _staging_for(device, lq.dtype, _crop_numel(lq, tiles, self.order))
+        self.dma = _dma_source(lq, device)
+        self.st = _staging_for(device, lq.dtype, _crop_numel(lq, tiles, self.order),
+                               host=not self.dma)
         self.copy_stream = torch.cuda.Stream(device)
+        if self.dma:
+            self.uploaded = {}
+            if self.order:
+                self._upload(0)
+            return
         self.pool = ThreadPoolExecutor(1)
         # a crop is copied by several host threads, split by frames (torch's copy releases
         # the GIL); the host's cores are shared by the ranks of this machine
@@ -267,11 +288,39 @@ class _TileLoader:
             j.result()
         return k
 
+    def _upload(self, k):
+        """Queue crop k on the side stream as one strided transfer from the pinned video
+        into device buffer k & 1, after the render of the tile that last used it."""
+        from . import _lib
+        x, y, w, h = self.tiles[self.order[k]]
+        b, st = k & 1, self.st
+        C, F, H, W = self.lq.shape
+        es = self.lq.element_size()
+        with torch.cuda.stream(self.copy_stream):
+            # after the tile that last read buffer b, and after any earlier upload into it
+            # (a render that stopped early can leave one in flight on its own side stream)
+            for prev in (st.used[b], st.up_done[b]):
+                if prev is not None:
+                    self.copy_stream.wait_event(prev)
+            _lib.call("fvb_copy_window_h2d", self.lq.data_ptr(), W * es, H, C * F, x * es, y,
+                      w * es, h, st.dev[b].data_ptr(), self.copy_stream.cuda_stream)
+            ev = torch.cuda.Event()
+            ev.record(self.copy_stream)
+        st.up_done[b] = ev
+        self.uploaded[k] = ev
+
     def get(self, k):
         """Crop of tile order[k] on the device, usable on the current stream."""
         x, y, w, h = self.tiles[self.order[k]]
         if self.direct:
             return self.lq[:, :, y:y + h, x:x + w].to(self.device)
+        if self.dma:
+            ev = self.uploaded.pop(k)
+            if k + 1 < len(self.order):
+                self._upload(k + 1)  # its buffer's last tile, k - 1, is marked done by now
+            torch.cuda.current_stream(self.device).wait_event(ev)
+            shp = self._shape(k)
+            return self.st.dev[k & 1][:shp[0] * shp[1] * shp[2] * shp[3]].view(shp)
         self.pending.result()
         b = k & 1
         shp = self._shape(k)
@@ -297,7 +346,7 @@ class _TileLoader:
         self.st.used[k & 1] = ev
 
     def close(self):
-        if not self.direct:
+        if not self.direct and not self.dma:
             if self.pending is not None:
                 self.pending.result()
             self.pool.shutdown()

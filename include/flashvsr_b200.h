@@ -252,6 +252,17 @@ FVB_API int fvb_window_partition(const void* x, int64_t x_ld, int64_t B, int64_t
                          int64_t Ww, int64_t C, int wf, int wh, int ww, int reverse, void* out,
                          fvb_stream_t stream);
 
+/* ------------------------------------------------- a17: tile crops of a host video
+ * Replaces the crop upload of render_tiled (tiling.py:190,
+ * `lq[:, :, y:y + h, x:x + w].to(dev, non_blocking=True)`) for a pinned host video: one
+ * strided copy-engine transfer, no host-side packing.  src holds `planes` planes of
+ * `src_rows` rows, `src_pitch` bytes per row; the window of `height` rows of `width_bytes`
+ * bytes at byte x_bytes of row y of every plane goes densely to dst
+ * ([planes, height, width_bytes]).  Asynchronous on `stream` when src is pinned. */
+FVB_API int fvb_copy_window_h2d(const void* src, int64_t src_pitch, int64_t src_rows,
+                                int64_t planes, int64_t x_bytes, int64_t y, int64_t width_bytes,
+                                int64_t height, void* dst, fvb_stream_t stream);
+
 /* ------------------------------------------------- a13: keep-mask selection
  * Replaces draft_block_mask (lcsa/reference.py:37-64), i.e. upstream
  * generate_draft_block_mask called at integrate.py:103-104:

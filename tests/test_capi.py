@@ -58,6 +58,12 @@ def test_host_validation_without_gpu():
         _lib.FVB_ERR_INVALID  # F=3 not divisible by 2
     assert lib.fvb_ln_modulate(None, None, None, 1, 4, 3000, 1e-6, None, None, None, None) == \
         _lib.FVB_ERR_INVALID  # D > 2048
+    # a crop window that leaves the plane is refused before any copy is queued
+    assert lib.fvb_copy_window_h2d(1, 7680, 2048, 255, 2 * 3000, 0, 1792, 768, 1, None) == \
+        _lib.FVB_ERR_INVALID  # x_bytes + width_bytes > pitch
+    assert "outside" in lib.fvb_last_error().decode()
+    assert lib.fvb_copy_window_h2d(1, 7680, 2048, 255, 0, 1500, 1792, 768, 1, None) == \
+        _lib.FVB_ERR_INVALID  # y + height > rows
     # empty problems are valid no-ops that need no device
     assert lib.fvb_gate_add(None, None, None, 0, 4, 8, None, None) == _lib.FVB_OK
     assert lib.fvb_fp8_gemm(None, None, 0, None, None, 0, None, 0, 8, 16, None, 0, None, None) == _lib.FVB_OK

@@ -1,7 +1,8 @@
 """render_tiled on the GPU: the prefetching host-crop path equals cropping on the device.
 
-The host video takes the pinned-staging / side-stream upload path of the tile loader; the
-same video already on the device is cropped there.  A deterministic per-tile pipe (a crop
+A pageable host video takes the pinned-staging / side-stream upload path of the tile
+loader, a pinned one the strided copy-engine path; the same video already on the device is
+cropped there.  A deterministic per-tile pipe (a crop
 transform, frame count changed like the real pipeline) makes any mix-up of tiles, buffers
 or stream ordering visible in the blended canvas.
 """
@@ -53,15 +54,19 @@ def test_tiled_pipe_graph_replay_equals_eager():
     assert graphed.tokens == eager.tokens
 
 
-def test_crop_staging_is_reused_across_renders():
-    """render_tiled keeps its pinned/device crop staging between calls (reserve_staging
-    allocates it ahead): back-to-back renders of different host videos through the same
-    buffers each equal the render of that video cropped on the device."""
+@pytest.mark.parametrize("pinned", [False, True])
+def test_crop_staging_is_reused_across_renders(pinned):
+    """render_tiled keeps its crop staging between calls (reserve_staging allocates it
+    ahead): back-to-back renders of different host videos through the same buffers each
+    equal the render of that video cropped on the device.  Pageable videos are packed into
+    pinned staging; pinned ones are copied by strided transfers (fvb_copy_window_h2d)."""
     from flashvsr_sm89_ops_b200 import tiling
     g = torch.Generator().manual_seed(9)
     C, F, H, W = 3, 5, 1536, 2688
     kw = dict(num_frames=F, tile_target=700_000, tile_threshold=700_000, device="cuda")
     videos = [(torch.rand(C, F, H, W, generator=g) * 2 - 1).to(torch.bfloat16) for _ in range(2)]
+    if pinned:
+        videos = [v.pin_memory() for v in videos]
     tiling.release_staging()
     tiling.reserve_staging(videos[0], tile_target=700_000, tile_threshold=700_000, device="cuda")
     st = next(iter(tiling._STAGING.values()))
