@@ -346,7 +346,14 @@ class _TileLoader:
         self.st.used[k & 1] = ev
 
     def close(self):
-        if not self.direct and not self.dma:
+        if self.dma:
+            # a render that stopped early may leave a prefetched crop in flight: finish it
+            # before the caller may free or refill the host video it reads
+            for ev in self.uploaded.values():
+                ev.synchronize()
+            self.uploaded.clear()
+            return
+        if not self.direct:
             if self.pending is not None:
                 self.pending.result()
             self.pool.shutdown()
